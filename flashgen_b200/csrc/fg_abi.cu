@@ -1,0 +1,210 @@
+// fg_abi.cu — C ABI entry points (include/flashgen_sampler.h).
+//
+// Host side only validates arguments, computes the shared-memory layout and
+// launches; it does no work proportional to batch * vocab, allocates nothing
+// and never synchronises the stream.
+#include <algorithm>
+#include <mutex>
+
+#include "fg_kernels.cuh"
+
+namespace {
+
+struct DevInfo {
+    int sms = 0;
+    int smem_optin = 0;
+    bool attr_set[3] = {false, false, false};
+    bool ok = false;
+};
+constexpr int kMaxDevices = 64;
+DevInfo g_dev[kMaxDevices];
+std::mutex g_mu;
+
+int device_info(DevInfo** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FG_EDEVICE;
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevInfo& d = g_dev[dev];
+    if (!d.ok) {
+        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return FG_EDEVICE;
+        if (cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+            return FG_EDEVICE;
+        d.ok = true;
+    }
+    *out = &d;
+    return FG_OK;
+}
+
+int elem_size(int dtype) {
+    switch (dtype) {
+        case FG_DTYPE_F32: return 4;
+        case FG_DTYPE_F16: return 2;
+        case FG_DTYPE_BF16: return 2;
+        default: return 0;
+    }
+}
+
+int bits_for(int64_t v) {  // smallest b >= 1 with v <= 2^b
+    int b = 1;
+    while ((int64_t(1) << b) < v) ++b;
+    return b;
+}
+
+template <int DT>
+int launch_sample(const fg::KParams& P, int smem, int grid, cudaStream_t st, DevInfo* d) {
+    auto kern = fg::fg_sample_kernel<DT>;
+    if (!d->attr_set[DT]) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->smem_optin) != cudaSuccess)
+            return FG_EDEVICE;
+        d->attr_set[DT] = true;
+    }
+    kern<<<grid, fg::NTHREADS, smem, st>>>(P);
+    return cudaGetLastError() == cudaSuccess ? FG_OK : FG_ELAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fg_version(void) { return 100; }
+
+const char* fg_strerror(int code) {
+    switch (code) {
+        case FG_OK: return "ok";
+        case FG_EINVAL: return "invalid argument";
+        case FG_ELAUNCH: return "kernel launch failed";
+        case FG_ENOTSUP: return "shape beyond on-chip limits of this build";
+        case FG_EDEVICE: return "device query or configuration failed";
+        default: return "unknown error";
+    }
+}
+
+int fg_sample(const FgSampleArgs* a, void* stream) {
+    if (a == nullptr) return FG_EINVAL;
+    const int esz = elem_size(a->dtype);
+    if (esz == 0 || a->logits == nullptr || a->batch < 0 || a->vocab < 1) return FG_EINVAL;
+    if (a->row_stride < a->vocab) return FG_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(a->logits) % esz) != 0) return FG_EINVAL;
+    if (a->temperature == nullptr || a->top_p == nullptr || a->top_k == nullptr || a->uniforms == nullptr ||
+        a->out_ids == nullptr)
+        return FG_EINVAL;
+    if ((a->hist_ids == nullptr) != (a->hist_offsets == nullptr)) return FG_EINVAL;
+    if (a->vocab_offset < 0) return FG_EINVAL;
+    const int64_t vtot = a->vocab_total > 0 ? a->vocab_total : a->vocab;
+    if (vtot < a->vocab_offset + a->vocab) return FG_EINVAL;
+    if (a->vocab > (1 << 28)) return FG_ENOTSUP;
+    if (a->batch == 0) return FG_OK;
+
+    DevInfo* d = nullptr;
+    int rc = device_info(&d);
+    if (rc != FG_OK) return rc;
+
+    fg::KParams P{};
+    P.logits = a->logits; P.row_stride = a->row_stride; P.batch = a->batch; P.vocab = a->vocab;
+    P.vocab_offset = a->vocab_offset; P.vocab_total = vtot;
+    P.hist_ids = a->hist_ids; P.hist_offsets = a->hist_offsets;
+    P.temperature = a->temperature; P.top_p = a->top_p; P.top_k = a->top_k;
+    P.rep = a->repetition_penalty; P.pres = a->presence_penalty; P.freq = a->frequency_penalty;
+    P.greedy = a->greedy; P.uniforms = a->uniforms;
+    P.out_ids = a->out_ids; P.out_status = a->out_status; P.out_probs = a->out_probs;
+    P.nwords = (a->vocab + 31) / 32;
+    const bool hist = a->hist_offsets != nullptr;
+    P.pen_possible = hist && (a->repetition_penalty || a->presence_penalty || a->frequency_penalty);
+    if (P.pen_possible && a->frequency_penalty != nullptr) {
+        if (a->hist_max_len < 0) return FG_EINVAL;
+        P.hu_cap = std::max(1, std::min(a->hist_max_len, a->vocab));
+    } else {
+        P.hu_cap = 0;
+    }
+    P.id_bits = bits_for(a->vocab);
+    P.mass_shift = 62 - P.id_bits;
+
+    const int tile_bytes = fg::TILE_ELEMS * esz;
+    int chosen = 0, smem = 0;
+    for (int ns = 16; ns >= 2; --ns) {
+        const fg::FixedLayout L = fg::fixed_layout(ns);
+        int off = L.end;
+        int ob = 0, op = 0, oc = 0;
+        if (P.pen_possible) {
+            off = fg::align_up_i(off, 16); ob = off; off += 4 * P.nwords;
+            if (P.hu_cap > 0) {
+                off = fg::align_up_i(off, 16); op = off; off += 4 * P.nwords;
+                off = fg::align_up_i(off, 16); oc = off; off += 4 * P.hu_cap;
+            }
+        }
+        off = fg::align_up_i(off, 128);
+        const int total = off + ns * tile_bytes;
+        if (total <= d->smem_optin) {
+            chosen = ns; smem = total;
+            P.off_bitmap = ob; P.off_prefix = op; P.off_counts = oc; P.off_ring = off;
+            break;
+        }
+    }
+    if (chosen == 0) return FG_ENOTSUP;
+    P.nstage = chosen;
+    const int grid = std::min(a->batch, d->sms);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    switch (a->dtype) {
+        case FG_DTYPE_F32: return launch_sample<FG_DTYPE_F32>(P, smem, grid, st, d);
+        case FG_DTYPE_F16: return launch_sample<FG_DTYPE_F16>(P, smem, grid, st, d);
+        default: return launch_sample<FG_DTYPE_BF16>(P, smem, grid, st, d);
+    }
+}
+
+int fg_argmax(const void* logits, int32_t dtype, int32_t batch, int32_t vocab, int64_t row_stride,
+              int64_t* out_ids, void* stream) {
+    const int esz = elem_size(dtype);
+    if (esz == 0 || logits == nullptr || out_ids == nullptr || batch < 0 || vocab < 1 || row_stride < vocab)
+        return FG_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(logits) % esz) != 0) return FG_EINVAL;
+    if (batch == 0) return FG_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    switch (dtype) {
+        case FG_DTYPE_F32: fg::fg_argmax_kernel<FG_DTYPE_F32><<<batch, 256, 0, st>>>(logits, vocab, row_stride, out_ids); break;
+        case FG_DTYPE_F16: fg::fg_argmax_kernel<FG_DTYPE_F16><<<batch, 256, 0, st>>>(logits, vocab, row_stride, out_ids); break;
+        default: fg::fg_argmax_kernel<FG_DTYPE_BF16><<<batch, 256, 0, st>>>(logits, vocab, row_stride, out_ids); break;
+    }
+    return cudaGetLastError() == cudaSuccess ? FG_OK : FG_ELAUNCH;
+}
+
+int fg_apply_repetition_penalty(void* logits, int32_t dtype, int32_t batch, int32_t vocab, int64_t row_stride,
+                                const int32_t* hist_ids, const int64_t* hist_offsets, const float* penalty,
+                                void* stream) {
+    const int esz = elem_size(dtype);
+    if (esz == 0 || logits == nullptr || batch < 0 || vocab < 1 || row_stride < vocab) return FG_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(logits) % esz) != 0) return FG_EINVAL;
+    if ((hist_ids == nullptr) != (hist_offsets == nullptr)) return FG_EINVAL;
+    if (batch == 0 || penalty == nullptr || hist_ids == nullptr) return FG_OK;
+    DevInfo* d = nullptr;
+    int rc = device_info(&d);
+    if (rc != FG_OK) return rc;
+    const int smem = 4 * ((vocab + 31) / 32);
+    if (smem > d->smem_optin) return FG_ENOTSUP;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    switch (dtype) {
+        case FG_DTYPE_F32: {
+            auto k = fg::fg_rep_penalty_kernel<FG_DTYPE_F32>;
+            if (smem > 48 * 1024) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e == cudaSuccess) k<<<batch, 256, smem, st>>>(logits, vocab, row_stride, hist_ids, hist_offsets, penalty);
+            break;
+        }
+        case FG_DTYPE_F16: {
+            auto k = fg::fg_rep_penalty_kernel<FG_DTYPE_F16>;
+            if (smem > 48 * 1024) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e == cudaSuccess) k<<<batch, 256, smem, st>>>(logits, vocab, row_stride, hist_ids, hist_offsets, penalty);
+            break;
+        }
+        default: {
+            auto k = fg::fg_rep_penalty_kernel<FG_DTYPE_BF16>;
+            if (smem > 48 * 1024) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e == cudaSuccess) k<<<batch, 256, smem, st>>>(logits, vocab, row_stride, hist_ids, hist_offsets, penalty);
+            break;
+        }
+    }
+    if (e != cudaSuccess) return FG_EDEVICE;
+    return cudaGetLastError() == cudaSuccess ? FG_OK : FG_ELAUNCH;
+}
+
+}  // extern "C"
