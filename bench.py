@@ -241,6 +241,7 @@ def main():
     out = torch.empty(B, dtype=torch.int64, device=dev)
     status = torch.empty(B, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
+    wspace = torch.zeros(_lib.FG_SAMPLE_WORKSPACE_BYTES // 4, dtype=torch.int32, device=dev)
 
     def make_args(i):
         a = _lib.FgSampleArgs()
@@ -255,6 +256,7 @@ def main():
         a.top_k, a.greedy = packed.top_k.data_ptr(), packed.greedy.data_ptr()
         a.uniforms = uni[i].data_ptr()
         a.out_ids, a.out_status = out.data_ptr(), status.data_ptr()
+        a.workspace = wspace.data_ptr()
         return a
 
     argv = [make_args(0), make_args(1)]

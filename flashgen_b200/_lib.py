@@ -53,7 +53,11 @@ class FgSampleArgs(ctypes.Structure):
         ("out_ids", ctypes.c_void_p),
         ("out_status", ctypes.c_void_p),
         ("out_probs", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
     ]
+
+
+FG_SAMPLE_WORKSPACE_BYTES = 256
 
 
 _lib = None

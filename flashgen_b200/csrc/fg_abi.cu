@@ -13,6 +13,7 @@ namespace {
 struct DevInfo {
     int sms = 0;
     int smem_optin = 0;
+    int smem_per_sm = 0;
     bool attr_set[3] = {false, false, false};
     bool ok = false;
 };
@@ -28,6 +29,8 @@ int device_info(DevInfo** out) {
     if (!d.ok) {
         if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return FG_EDEVICE;
         if (cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+            return FG_EDEVICE;
+        if (cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess)
             return FG_EDEVICE;
         d.ok = true;
     }
@@ -56,6 +59,9 @@ int launch_sample(const fg::KParams& P, int smem, int grid, cudaStream_t st, Dev
     if (!d->attr_set[DT]) {
         std::lock_guard<std::mutex> lk(g_mu);
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->smem_optin) != cudaSuccess)
+            return FG_EDEVICE;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return FG_EDEVICE;
         d->attr_set[DT] = true;
     }
@@ -87,7 +93,7 @@ int fg_sample(const FgSampleArgs* a, void* stream) {
     if (a->row_stride < a->vocab) return FG_EINVAL;
     if ((reinterpret_cast<uintptr_t>(a->logits) % esz) != 0) return FG_EINVAL;
     if (a->temperature == nullptr || a->top_p == nullptr || a->top_k == nullptr || a->uniforms == nullptr ||
-        a->out_ids == nullptr)
+        a->out_ids == nullptr || a->workspace == nullptr)
         return FG_EINVAL;
     if ((a->hist_ids == nullptr) != (a->hist_offsets == nullptr)) return FG_EINVAL;
     if (a->vocab_offset < 0) return FG_EINVAL;
@@ -108,10 +114,11 @@ int fg_sample(const FgSampleArgs* a, void* stream) {
     P.rep = a->repetition_penalty; P.pres = a->presence_penalty; P.freq = a->frequency_penalty;
     P.greedy = a->greedy; P.uniforms = a->uniforms;
     P.out_ids = a->out_ids; P.out_status = a->out_status; P.out_probs = a->out_probs;
+    P.ws = reinterpret_cast<fg::Workspace*>(a->workspace);
     P.nwords = (a->vocab + 31) / 32;
     const bool hist = a->hist_offsets != nullptr;
     P.pen_possible = hist && (a->repetition_penalty || a->presence_penalty || a->frequency_penalty);
-    if (P.pen_possible && a->frequency_penalty != nullptr) {
+    if (P.pen_possible) {
         if (a->hist_max_len < 0) return FG_EINVAL;
         P.hu_cap = std::max(1, std::min(a->hist_max_len, a->vocab));
     } else {
@@ -120,30 +127,41 @@ int fg_sample(const FgSampleArgs* a, void* stream) {
     P.id_bits = bits_for(a->vocab);
     P.mass_shift = 62 - P.id_bits;
 
-    const int tile_bytes = fg::TILE_ELEMS * esz;
-    int chosen = 0, smem = 0;
-    for (int ns = 16; ns >= 2; --ns) {
-        const fg::FixedLayout L = fg::fixed_layout(ns);
-        int off = L.end;
-        int ob = 0, op = 0, oc = 0;
-        if (P.pen_possible) {
-            off = fg::align_up_i(off, 16); ob = off; off += 4 * P.nwords;
-            if (P.hu_cap > 0) {
-                off = fg::align_up_i(off, 16); op = off; off += 4 * P.nwords;
-                off = fg::align_up_i(off, 16); oc = off; off += 4 * P.hu_cap;
+    // two CTAs per SM when one fits in half of the SM's shared memory (with at
+    // least four 8 KB stages); otherwise one CTA per SM with a deeper ring
+    int chosen = 0, smem = 0, per_sm = 1;
+    for (int pass = 0; pass < 2 && chosen == 0; ++pass) {
+        const int limit = pass == 0 ? (d->smem_per_sm / 2 - 1024) : d->smem_optin;
+        const int min_ns = pass == 0 ? 4 : 2;
+        for (int ns = 12; ns >= min_ns; --ns) {
+            int off = fg::head_bytes(ns);
+            const int ob = off; off += 2 * 8 * fg::NB;
+            const int oc = off; off += 2 * 4 * fg::NB;
+            off = fg::align_up_i(off, 16);
+            const int ok = off; off += 4 * fg::CAND_CAP;
+            const int oi = off; off += 4 * fg::CAND_CAP;
+            int obm = 0, opf = 0, ocn = 0, osv = 0, osc = 0;
+            if (P.pen_possible) {
+                off = fg::align_up_i(off, 16); obm = off; off += 4 * P.nwords;
+                off = fg::align_up_i(off, 16); opf = off; off += 2 * ((P.nwords + 1) / 2);
+                off = fg::align_up_i(off, 16); ocn = off; off += 4 * P.hu_cap;
+                off = fg::align_up_i(off, 16); osv = off; off += 4 * P.hu_cap;
+                off = fg::align_up_i(off, 16); osc = off; off += 4 * P.hu_cap;
             }
-        }
-        off = fg::align_up_i(off, 128);
-        const int total = off + ns * tile_bytes;
-        if (total <= d->smem_optin) {
-            chosen = ns; smem = total;
-            P.off_bitmap = ob; P.off_prefix = op; P.off_counts = oc; P.off_ring = off;
-            break;
+            off = fg::align_up_i(off, 128);
+            const int total = off + ns * fg::TILE_BYTES;
+            if (total <= limit) {
+                chosen = ns; smem = total; per_sm = pass == 0 ? 2 : 1;
+                P.off_bins = ob; P.off_cnts = oc; P.off_ckey = ok; P.off_cid = oi;
+                P.off_bitmap = obm; P.off_prefix = opf; P.off_counts = ocn; P.off_sval = osv; P.off_scol = osc;
+                P.off_ring = off;
+                break;
+            }
         }
     }
     if (chosen == 0) return FG_ENOTSUP;
     P.nstage = chosen;
-    const int grid = std::min(a->batch, d->sms);
+    const int grid = std::min(a->batch, d->sms * per_sm);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     switch (a->dtype) {
         case FG_DTYPE_F32: return launch_sample<FG_DTYPE_F32>(P, smem, grid, st, d);

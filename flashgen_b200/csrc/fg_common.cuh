@@ -160,6 +160,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         }
     }
 }
+// Wait for phase `parity` of `bar` for at most `limit_ns`; returns false on expiry.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_test(bar, parity))
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+    return true;
+}
 // 1-D bulk copy global -> shared, completion counted on `bar` (complete_tx).
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -8,59 +8,230 @@
 
 namespace fg {
 
+constexpr float L2E = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2_approx(float v) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(v));
+    return y;
+}
+
 // ---------------------------------------------------------------------------
-// History prologue: bitmap of this row's history ids restricted to the
-// columns of this call; when a frequency penalty is set, also the rank of
-// every set bit (word prefix of popcounts) and the count of each id.
+// Chunk helpers (one 16-byte chunk = VEC elements)
 // ---------------------------------------------------------------------------
+template <int DT> struct Neg;  // 16-byte pattern of -inf elements
+template <> struct Neg<FG_DTYPE_F32> { static constexpr uint32_t W = 0xFF800000u; };
+template <> struct Neg<FG_DTYPE_F16> { static constexpr uint32_t W = 0xFC00FC00u; };
+template <> struct Neg<FG_DTYPE_BF16> { static constexpr uint32_t W = 0xFF80FF80u; };
+
+__device__ __forceinline__ uint32_t& word_of(uint4& v, int q) {
+    return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
+}
+__device__ __forceinline__ uint32_t word_get(const uint4& v, int q) {
+    return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
+}
+template <int DT>
+__device__ __forceinline__ float elem_get(const uint4& v, int e) {
+    if constexpr (DT == FG_DTYPE_F32) {
+        return __uint_as_float(word_get(v, e));
+    } else {
+        const uint32_t w = word_get(v, e >> 1);
+        const uint16_t h = (e & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xffffu);
+        if constexpr (DT == FG_DTYPE_BF16) return __uint_as_float(uint32_t(h) << 16);
+        else return __half2float(__ushort_as_half(h));
+    }
+}
+template <int DT>
+__device__ __forceinline__ void elem_mask(uint4& v, int e) {
+    if constexpr (DT == FG_DTYPE_F32) {
+        word_of(v, e) = Neg<DT>::W;
+    } else {
+        uint32_t& w = word_of(v, e >> 1);
+        w = (e & 1) ? ((w & 0x0000ffffu) | (Neg<DT>::W & 0xffff0000u)) : ((w & 0xffff0000u) | (Neg<DT>::W & 0xffffu));
+    }
+}
+
+// NaN-propagating max over CPT chunks (pairwise tree; packed pairs for 16-bit types).
+template <int DT>
+__device__ __forceinline__ float chunk_max1(const uint4& v) {
+    if constexpr (DT == FG_DTYPE_F32) {
+        return fmax_nan(fmax_nan(__uint_as_float(v.x), __uint_as_float(v.y)),
+                        fmax_nan(__uint_as_float(v.z), __uint_as_float(v.w)));
+    } else if constexpr (DT == FG_DTYPE_BF16) {
+        const __nv_bfloat162 a = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&v.x),
+                                             *reinterpret_cast<const __nv_bfloat162*>(&v.y));
+        const __nv_bfloat162 b = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&v.z),
+                                             *reinterpret_cast<const __nv_bfloat162*>(&v.w));
+        const __nv_bfloat162 m = __hmax2_nan(a, b);
+        return fmax_nan(__low2float(m), __high2float(m));
+    } else {
+        const __half2 a = __hmax2_nan(*reinterpret_cast<const __half2*>(&v.x), *reinterpret_cast<const __half2*>(&v.y));
+        const __half2 b = __hmax2_nan(*reinterpret_cast<const __half2*>(&v.z), *reinterpret_cast<const __half2*>(&v.w));
+        const __half2 m = __hmax2_nan(a, b);
+        return fmax_nan(__low2float(m), __high2float(m));
+    }
+}
+template <int DT>
+__device__ __forceinline__ float chunks_max(const uint4 (&v)[CPT]) {
+    float m = chunk_max1<DT>(v[0]);
+#pragma unroll
+    for (int j = 1; j < CPT; ++j) m = fmax_nan(m, chunk_max1<DT>(v[j]));
+    return m;
+}
+// Minimum over CPT chunks (NaN ignored by fminf).
+template <int DT>
+__device__ __forceinline__ float chunks_min(const uint4 (&v)[CPT]) {
+    float r = INFINITY;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+        if constexpr (DT == FG_DTYPE_F32) {
+            r = fminf(r, fminf(fminf(__uint_as_float(v[j].x), __uint_as_float(v[j].y)),
+                               fminf(__uint_as_float(v[j].z), __uint_as_float(v[j].w))));
+        } else if constexpr (DT == FG_DTYPE_BF16) {
+            const __nv_bfloat162 m = __hmin2(__hmin2(*reinterpret_cast<const __nv_bfloat162*>(&v[j].x),
+                                                     *reinterpret_cast<const __nv_bfloat162*>(&v[j].y)),
+                                             __hmin2(*reinterpret_cast<const __nv_bfloat162*>(&v[j].z),
+                                                     *reinterpret_cast<const __nv_bfloat162*>(&v[j].w)));
+            r = fminf(r, fminf(__low2float(m), __high2float(m)));
+        } else {
+            const __half2 m = __hmin2(__hmin2(*reinterpret_cast<const __half2*>(&v[j].x), *reinterpret_cast<const __half2*>(&v[j].y)),
+                                      __hmin2(*reinterpret_cast<const __half2*>(&v[j].z), *reinterpret_cast<const __half2*>(&v[j].w)));
+            r = fminf(r, fminf(__low2float(m), __high2float(m)));
+        }
+    }
+    return r;
+}
+
+// z += sum_e 2^(x_e * c - zmc) over every element of the chunks (two accumulators).
+template <int DT>
+__device__ __forceinline__ void chunks_sumexp(const uint4 (&v)[CPT], float c, float nzmc, float& z0, float& z1) {
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t w = word_get(v[j], q);
+            if constexpr (DT == FG_DTYPE_F32) {
+                if (q & 1) z1 += ex2_approx(__fmaf_rn(__uint_as_float(w), c, nzmc));
+                else z0 += ex2_approx(__fmaf_rn(__uint_as_float(w), c, nzmc));
+            } else {
+                float lo, hi;
+                if constexpr (DT == FG_DTYPE_BF16) {
+                    lo = __uint_as_float(w << 16); hi = __uint_as_float(w & 0xffff0000u);
+                } else {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+                    lo = f.x; hi = f.y;
+                }
+                z0 += ex2_approx(__fmaf_rn(lo, c, nzmc));
+                z1 += ex2_approx(__fmaf_rn(hi, c, nzmc));
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// History prologue: bitmap of this row's history columns, the ascending list
+// of distinct history columns (scol), a popcount prefix per 64-column pair of
+// bitmap words (so a column's rank — its index in scol — costs three shared
+// loads), and per-rank counts when a frequency penalty is set.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t hist_rank(const Smem& s, uint32_t c) {
+    const uint32_t w = c >> 5;
+    uint32_t r = s.prefix[w >> 1] + __popc(s.bitmap[w] & ((1u << (c & 31)) - 1u));
+    if (w & 1u) r += __popc(s.bitmap[w - 1]);
+    return r;
+}
+
 __device__ void history_prologue(const KParams& P, const Smem& s, const RowParams& p, int r, int tid) {
     const int nw = P.nwords;
+    const int npair = (nw + 1) >> 1;
+    const int lane = tid & 31;
     for (int w = tid; w < nw; w += NCT) s.bitmap[w] = 0u;
     csync();
     const int64_t h0 = __ldg(P.hist_offsets + r), h1 = __ldg(P.hist_offsets + r + 1);
+    constexpr int HB = 4;   // ids per thread per batch, loaded together
     int bad = 0;
-    for (int64_t i = h0 + tid; i < h1; i += NCT) {
-        const int64_t gid = __ldg(P.hist_ids + i);
-        if (gid < 0 || gid >= P.vocab_total) { bad = 1; continue; }
-        const int64_t c = gid - P.vocab_offset;
-        if (c >= 0 && c < P.vocab) atomicOr(&s.bitmap[c >> 5], 1u << (c & 31));
+    for (int64_t b0 = h0; b0 < h1; b0 += (int64_t)NCT * HB) {
+        int32_t ids[HB];
+#pragma unroll
+        for (int j = 0; j < HB; ++j) {
+            const int64_t i = b0 + tid + (int64_t)j * NCT;
+            ids[j] = i < h1 ? __ldg(P.hist_ids + i) : -1;
+        }
+#pragma unroll
+        for (int j = 0; j < HB; ++j) {
+            const int64_t i = b0 + tid + (int64_t)j * NCT;
+            if (i >= h1) continue;
+            const int64_t gid = ids[j];
+            if (gid < 0 || gid >= P.vocab_total) { bad = 1; continue; }
+            const int64_t c = gid - P.vocab_offset;
+            if (c >= 0 && c < P.vocab) {
+                const uint32_t bit = 1u << (c & 31);
+                if (!(s.bitmap[c >> 5] & bit)) atomicOr(&s.bitmap[c >> 5], bit);
+            }
+        }
     }
     if (bad) atomicOr(&s.ctl->status, FG_ROW_BAD_HISTORY);
     csync();
-    if (!p.freq_on) return;
-    // word prefix of popcounts: thread t owns a contiguous range of words
-    const int wpt = (nw + NCT - 1) / NCT;
-    const int w0 = tid * wpt, w1 = min(nw, w0 + wpt);
+    // thread t owns the word pairs [q0, q1): prefix counts and the scol entries
+    const int ppt = (npair + NCT - 1) / NCT;
+    const int q0 = tid * ppt, q1 = min(npair, q0 + ppt);
     uint32_t local = 0;
-    for (int w = w0; w < w1; ++w) local += __popc(s.bitmap[w]);
+    for (int q = q0; q < q1; ++q) {
+        local += __popc(s.bitmap[2 * q]);
+        if (2 * q + 1 < nw) local += __popc(s.bitmap[2 * q + 1]);
+    }
     uint32_t total;
     uint32_t run = cons_excl_scan_u32(local, total, s, tid);
-    for (int w = w0; w < w1; ++w) { s.prefix[w] = run; run += __popc(s.bitmap[w]); }
-    const uint32_t U = min(total, (uint32_t)P.hu_cap);
-    for (uint32_t i = tid; i < U; i += NCT) s.counts[i] = 0u;
-    if (tid == 0 && total > (uint32_t)P.hu_cap) atomicOr(&s.ctl->status, FG_ROW_BAD_PARAM);
+    const uint32_t cap = (uint32_t)P.hu_cap;
+    for (int q = q0; q < q1; ++q) {
+        s.prefix[q] = (uint16_t)run;
+        run += __popc(s.bitmap[2 * q]) + (2 * q + 1 < nw ? __popc(s.bitmap[2 * q + 1]) : 0);
+    }
     csync();
-    for (int64_t i = h0 + tid; i < h1; i += NCT) {
-        const int64_t gid = __ldg(P.hist_ids + i);
-        if (gid < 0 || gid >= P.vocab_total) continue;
-        const int64_t c = gid - P.vocab_offset;
-        if (c < 0 || c >= P.vocab) continue;
-        const uint32_t w = (uint32_t)(c >> 5), b = (uint32_t)(c & 31);
-        const uint32_t rank = s.prefix[w] + __popc(s.bitmap[w] & ((1u << b) - 1u));
-        if (rank < (uint32_t)P.hu_cap) atomicAdd(&s.counts[rank], 1u);
+    // ascending list of distinct columns: warp-parallel over words (a lane per bit)
+    for (int w0 = (tid >> 5); w0 < nw; w0 += NCW) {
+        const uint32_t bits = s.bitmap[w0];
+        if (bits == 0u) continue;
+        if ((bits >> lane) & 1u) {
+            const uint32_t rk = hist_rank(s, (uint32_t)(w0 * 32 + lane));
+            if (rk < cap) s.scol[rk] = (uint32_t)(w0 * 32 + lane);
+        }
+    }
+    const uint32_t U = min(total, cap);
+    if (tid == 0) {
+        s.ctl->nunique = U;
+        if (total > cap || total > 65535u) atomicOr(&s.ctl->status, FG_ROW_BAD_PARAM);
+    }
+    for (uint32_t i = tid; i < U; i += NCT) s.sval[i] = -INFINITY;
+    if (p.freq_on) {
+        for (uint32_t i = tid; i < U; i += NCT) s.counts[i] = 0u;
+        csync();
+        for (int64_t b0 = h0; b0 < h1; b0 += (int64_t)NCT * HB) {
+            int32_t ids[HB];
+#pragma unroll
+            for (int j = 0; j < HB; ++j) {
+                const int64_t i = b0 + tid + (int64_t)j * NCT;
+                ids[j] = i < h1 ? __ldg(P.hist_ids + i) : -1;
+            }
+#pragma unroll
+            for (int j = 0; j < HB; ++j) {
+                const int64_t i = b0 + tid + (int64_t)j * NCT;
+                const int64_t gid = ids[j];
+                const int64_t c = gid - P.vocab_offset;
+                bool v = i < h1 && gid >= 0 && gid < P.vocab_total && c >= 0 && c < P.vocab;
+                const uint32_t rk = v ? hist_rank(s, (uint32_t)c) : 0u;
+                v = v && rk < U;
+                agg_add<true>(s.counts, nullptr, v, rk, 0ull, lane);
+            }
+        }
     }
     csync();
 }
 
-// Penalised value of column c (its history bit is known to be set).
-__device__ __forceinline__ float penalize(const RowParams& p, const Smem& s, int c, float x) {
+// Penalised value of the history column with the given rank.
+__device__ __forceinline__ float penalize(const RowParams& p, const Smem& s, uint32_t rank, float x) {
     if (p.rep_on) x = (x > 0.0f) ? __fdiv_rn(x, p.rep) : __fmul_rn(x, p.rep);
-    if (p.freq_on) {
-        const uint32_t w = (uint32_t)c >> 5, b = (uint32_t)c & 31;
-        const uint32_t rank = s.prefix[w] + __popc(s.bitmap[w] & ((1u << b) - 1u));
-        const float cnt = (float)s.counts[rank];
-        x = __fsub_rn(x, __fmul_rn(p.freq, cnt));
-    }
+    if (p.freq_on) x = __fsub_rn(x, __fmul_rn(p.freq, (float)s.counts[rank]));
     if (p.pres_on) x = __fsub_rn(x, p.pres);
     return x;
 }
@@ -71,117 +242,102 @@ __device__ __forceinline__ uint32_t hist_bits(const Smem& s, int nwords, int c0,
     const uint32_t hi = (b + n > 32 && w + 1 < nwords) ? s.bitmap[w + 1] : 0u;
     return __funnelshift_r(lo, hi, b) & ((1u << n) - 1u);
 }
-template <int N>
-__device__ __forceinline__ void penalize_chunk(const RowParams& p, const Smem& s, int nwords, int c0, float (&x)[N]) {
-    uint32_t bits = hist_bits(s, nwords, c0, N);
-    while (bits) {
-        const int e = __ffs(bits) - 1;
-        bits &= bits - 1;
-#pragma unroll
-        for (int j = 0; j < N; ++j) if (j == e) x[j] = penalize(p, s, c0 + j, x[j]);
-    }
-}
-
-__device__ __forceinline__ float ex2_approx(float v) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(v));
-    return y;
-}
 
 // ---------------------------------------------------------------------------
-// Streaming state of one consumer thread
+// Per-thread streaming state
 // ---------------------------------------------------------------------------
 struct Stream {
-    float tmax;    // NaN-propagating max of penalised x
-    float zm;      // running max used by the online sum-exp
-    float zmc;     // fl(zm * c)
-    float z;       // sum of 2^(x*c - zmc)
-    float xmin;    // register copy of the candidate filter
+    float tmax;           // NaN-propagating max of penalised x (whole row)
+    float imax;           // max over the streamed interior (greedy rows)
+    int itile;            // first tile where imax was reached
+    float tmin;           // min over the row (rows with a sum-exp)
+    float zm, nzmc;       // running max for the sum-exp and -fl(zm * c)
+    float z0, z1;         // sum of 2^(x*c + nzmc)
+    float xmin;           // register copy of the candidate filter
+    float bestv;          // greedy rows: best element outside the streamed interior
+    uint32_t bestc;
     bool cand;
+    uint32_t base;        // candidates before the current window
+    uint32_t win;         // window index (counter slot = win % 3)
 };
 
-// Process N values x[0..N) of columns cols(e) = c0 + e (valid bits in vmask).
-template <int N>
-__device__ __forceinline__ void process(const RowParams& p, const Smem& s, Stream& st, const float (&x)[N],
-                                        int c0, uint32_t vmask, int lane) {
-    float cmax = -INFINITY;
-#pragma unroll
-    for (int e = 0; e < N; ++e) if (vmask >> e & 1u) cmax = fmax_nan(cmax, x[e]);
-    st.tmax = fmax_nan(st.tmax, cmax);
-    if (p.mode == MODE_NUCLEUS) {
-        if (cmax > st.zm) {
-            const float nmc = cmax * p.c;
-            st.z *= ex2_approx(st.zmc - nmc);
-            st.zm = cmax; st.zmc = nmc;
+// Warp-aggregated append of the items selected by `pick` (bit i selects item i;
+// item(i, key, col) returns them).
+template <class Item>
+__device__ __forceinline__ void warp_append(const Smem& s, Stream& st, uint32_t pick, int lane, Item&& item) {
+    const uint32_t cnt = __popc(pick);
+    const uint32_t incl = warp_incl_scan_u32(cnt, lane);
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    if (total == 0) return;
+    const int slot = (int)(st.win % 3u);
+    uint32_t base = 0;
+    if (lane == 31) base = atomicAdd(&s.ctl->wcnt[slot], total);
+    base = __shfl_sync(0xffffffffu, base, 31) + st.base;
+    uint32_t pos = base + incl - cnt;
+    uint32_t kmax = 0, kmin = 0xffffffffu;
+    bool ovf = false;
+    while (pick) {
+        const int i = __ffs(pick) - 1;
+        pick &= pick - 1;
+        uint32_t key, col;
+        item(i, key, col);
+        if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = key; s.cid[pos] = col; } else ovf = true;
+        ++pos;
+        kmax = max(kmax, key); kmin = min(kmin, key);
+    }
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    kmin = __reduce_min_sync(0xffffffffu, kmin);
+    if (__any_sync(0xffffffffu, ovf) && lane == 0) s.ctl->ovf[slot] = 1;
+    if (lane == 0) { atomicMax(&s.ctl->hikey, kmax); atomicMin(&s.ctl->lokey, kmin); }
+}
+
+// One element outside the streamed interior (ragged columns, merged history).
+__device__ __forceinline__ void process_one(const RowParams& p, const Smem& s, Stream& st, float x,
+                                            uint32_t col, bool valid, int lane) {
+    if (valid) {
+        st.tmax = fmax_nan(st.tmax, x);
+        if (p.mode == MODE_GREEDY && (x > st.bestv || (x == st.bestv && col < st.bestc))) { st.bestv = x; st.bestc = col; }
+        if (p.zsum) {
+            st.tmin = fminf(st.tmin, x);
+            if (x > st.zm) {
+                const float nn = -(x * p.c);
+                const float f = ex2_approx(nn - st.nzmc);
+                st.z0 *= f; st.z1 *= f;
+                st.zm = x; st.nzmc = nn;
+            }
+            st.z0 += ex2_approx(__fmaf_rn(x, p.c, st.nzmc));
         }
-#pragma unroll
-        for (int e = 0; e < N; ++e)
-            if (vmask >> e & 1u) st.z += ex2_approx(__fmaf_rn(x[e], p.c, -st.zmc));
     }
     if (st.cand) {
-        uint32_t pm = 0;
-#pragma unroll
-        for (int e = 0; e < N; ++e) if ((vmask >> e & 1u) && x[e] >= st.xmin) pm |= 1u << e;
-        if (__any_sync(0xffffffffu, pm)) {
-            const uint32_t cnt = __popc(pm);
-            const uint32_t incl = warp_incl_scan_u32(cnt, lane);
-            const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-            uint32_t base = 0;
-            if (lane == 31) base = atomicAdd(&s.ctl->n, total);
-            base = __shfl_sync(0xffffffffu, base, 31);
-            uint32_t pos = base + incl - cnt;
-            uint32_t kmax = 0;
-#pragma unroll
-            for (int e = 0; e < N; ++e) {
-                if (pm >> e & 1u) {
-                    const uint32_t k = fkey(x[e]);
-                    if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = k; s.cid[pos] = (uint32_t)(c0 + e); }
-                    ++pos;
-                    kmax = max(kmax, k);
-                }
-            }
-            kmax = __reduce_max_sync(0xffffffffu, kmax);
-            if (lane == 0) atomicMax(&s.ctl->hikey, kmax);
+        const uint32_t pick = (valid && x >= st.xmin) ? 1u : 0u;
+        if (__any_sync(0xffffffffu, pick)) {
+            const uint32_t key = fkey(x);
+            warp_append(s, st, pick, lane, [&](int, uint32_t& k, uint32_t& c) { k = key; c = col; });
         }
     }
 }
 
 // ---------------------------------------------------------------------------
-// Compaction: raise xmin to a valid lower bound of the K-th largest value and
-// drop candidates below it (stable, in place).
+// Compaction: exact K-th largest candidate key -> xmin; drop keys below it
+// (stable, in place). Returns the new candidate count.
 // ---------------------------------------------------------------------------
-__device__ void compact(const RowParams& p, const Smem& s, int tid, uint32_t n) {
+__device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t n) {
     RowCtl* ctl = s.ctl;
-    const uint32_t lo = fkey(ctl->xmin);
-    const uint32_t hi = ctl->hikey;
-    const uint32_t span = hi >= lo ? hi - lo : 0u;
-    const int shift = span < (uint32_t)NBINS ? 0 : (32 - __clz(span) - 8);
-    if (tid < NBINS) s.cnts[tid] = 0u;
-    csync();
-    for (uint32_t i = tid; i < n; i += NCT) {
-        const uint32_t k = s.ckey[i];
-        if (k >= lo) atomicAdd(&s.cnts[(k - lo) >> shift], 1u);
-    }
-    csync();
-    if (tid < 32) {
-        const int lane = tid;
-        uint32_t v[8], lsum = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) { v[j] = s.cnts[NBINS - 1 - (lane * 8 + j)]; lsum += v[j]; }
-        const uint32_t incl = warp_incl_scan_u32(lsum, lane);
-        const uint32_t excl = incl - lsum;
-        const uint32_t K = (uint32_t)p.K;
-        const bool mine = excl < K && K <= incl;
-        const uint32_t bal = __ballot_sync(0xffffffffu, mine);
-        if (bal != 0 && lane == __ffs(bal) - 1) {
-            uint32_t c = excl;
-            int jj = 0;
-            for (; jj < 7; ++jj) { c += v[jj]; if (c >= K) break; }
-            const uint32_t b = (uint32_t)(NBINS - 1 - (lane * 8 + jj));
-            const uint32_t tau_key = lo + (b << shift);
-            const float xm = xmin_for(p, funkey(tau_key));
-            if (xm > ctl->xmin) ctl->xmin = xm;
-        }
+    const uint32_t lo = ctl->lokey, hi = ctl->hikey;
+    if (n <= (uint32_t)p.K || lo > hi) return n;
+    const SelOut so = block_select<true, true>(
+        [&](auto&& f) {
+            for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+                const uint32_t i = i0 + tid;
+                f(i < n, i < n ? s.ckey[i] : 0u, 1ull);
+            }
+        },
+        (uint64_t)(p.K - 1), lo, varying_bits(lo, hi), s, tid);
+    if (!so.ok) return n;
+    if (tid == 0) {
+        const float xm = xmin_for(p, funkey(so.key));
+        if (xm > ctl->xmin) ctl->xmin = xm;
+        ctl->lokey = fkey(ctl->xmin);
     }
     csync();
     const uint32_t kmin = fkey(ctl->xmin);
@@ -204,15 +360,32 @@ __device__ void compact(const RowParams& p, const Smem& s, int tid, uint32_t n) 
         out += total;
         csync();
     }
-    if (tid == 0) {
-        ctl->n = out;
-        if (out > (uint32_t)HWM) { ctl->cand_on = 0; ctl->general = 1; }
-    }
+    return out;
+}
+
+// End of a candidate window: uniform candidate count, compaction when the
+// buffer passed `limit`.
+__device__ __forceinline__ void window_check(const RowParams& p, const Smem& s, int tid, Stream& st, uint32_t limit) {
     csync();
+    const int slot = (int)(st.win % 3u);
+    uint32_t n = st.base + s.ctl->wcnt[slot];
+    const bool ovf = s.ctl->ovf[slot] != 0;
+    if (tid == 0) { s.ctl->wcnt[(slot + 2) % 3] = 0u; s.ctl->ovf[(slot + 2) % 3] = 0; }
+    st.win += 1;
+    if (st.cand) {
+        if (ovf) {
+            st.cand = false;
+        } else if (n > limit) {
+            n = compact(p, s, tid, n);
+            if (n > limit) st.cand = false;
+        }
+        st.xmin = s.ctl->xmin;
+    }
+    st.base = n;
 }
 
 // ---------------------------------------------------------------------------
-// Whole-row enumeration from global memory (general path).
+// Whole-row enumeration from global memory (L2) for the multi-pass paths.
 // f(col, x) with x the penalised fp32 value.
 // ---------------------------------------------------------------------------
 template <int DT, class F>
@@ -222,331 +395,762 @@ __device__ __forceinline__ void for_row(const KParams& P, const Smem& s, const R
     constexpr int ESZ = E::SIZE, VEC = E::VEC;
     const uint8_t* row = reinterpret_cast<const uint8_t*>(P.logits) + (int64_t)r * P.row_stride * ESZ;
     const int nh = g.head, nt = P.vocab - g.tail0;
-    if (tid < nh + nt) {
+    if (tid < 32 && nh + nt > 0) {
+        const bool valid = tid < nh + nt;
         const int c = tid < nh ? tid : g.tail0 + (tid - nh);
-        float x = E::load(row, c);
-        if (p.pen && (hist_bits(s, P.nwords, c, 1) & 1u)) x = penalize(p, s, c, x);
-        f(c, x);
+        float x = -INFINITY;
+        if (valid) {
+            x = E::load(row, c);
+            if (p.pen && (hist_bits(s, P.nwords, c, 1) & 1u)) x = penalize(p, s, hist_rank(s, (uint32_t)c), x);
+        }
+        f(valid, valid ? c : 0, x);
     }
     const int64_t nchunk = g.interior_bytes / 16;
-    for (int64_t ch = tid; ch < nchunk; ch += NCT) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(g.interior) + ch);
+    for (int64_t ch0 = 0; ch0 < nchunk; ch0 += NCT) {
+        const int64_t ch = ch0 + tid;
+        const bool valid = ch < nchunk;
         float x[VEC];
-        E::unpack(v, x);
-        const int c0 = g.head + (int)(ch * (16 / ESZ));
-        if (p.pen) penalize_chunk<VEC>(p, s, P.nwords, c0, x);
+        int c0 = 0;
+        if (valid) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(g.interior) + ch);
+            E::unpack(v, x);
+            c0 = g.head + (int)(ch * VEC);
+            if (p.pen) {
+                uint32_t bits = hist_bits(s, P.nwords, c0, VEC);
+                while (bits) {
+                    const int e = __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    const uint32_t rk = hist_rank(s, (uint32_t)(c0 + e));
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) f(c0 + e, x[e]);
+                    for (int j = 0; j < VEC; ++j)
+                        if (j == e) x[j] = penalize(p, s, rk, x[j]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) x[e] = -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) f(valid, c0 + e, x[e]);
     }
 }
 
-__device__ __forceinline__ uint64_t mass_q(float y, float My, float scale) {
-    const float e = expf(y - My);
-    return (uint64_t)__float2ull_rn(e * scale);
-}
+__device__ __forceinline__ uint64_t q_of(float e, float scale) { return (uint64_t)__float2ull_rn(e * scale); }
+// Fast mass of a value y outside the candidate set (a function of y alone, so
+// equal values get equal masses).
+__device__ __forceinline__ float efast(float y, float My) { return ex2_approx((y - My) * L2E); }
 
 // ---------------------------------------------------------------------------
-// Sampling decision over an abstract element set.
-//   enumerate(f): f(ykey, col, q, keep_k) for the thread's elements
-// Returns the chosen column (or -1 if the set is empty), fills probs.
+// Locate, over the region R of the row (elements whose y-key lies in
+// [rlo, rhi]), the element where the cumulative fast mass in descending y
+// order crosses `target` (clamped to the region's total).
+//   level 0: NB bins linear in y over [ylo, yhi] (values at or below ylo,
+//            whose masses are zero at this precision, share bin 0);
+//   if the crossing bin holds more elements than the buffer can take, its key
+//   range is refined with 8-bit radix passes;
+//   the crossing set is collected into [slot0, CAND_CAP) and the element is
+//   selected exactly among it.
 // ---------------------------------------------------------------------------
-template <class Enum>
-__device__ int decide(const KParams& P, const Smem& s, const RowParams& p, int r, int tid,
-                      Enum&& enumerate, bool topk_done, uint32_t ykK, double Qn_override, bool* not_covered) {
-    *not_covered = false;
-    // kept_k predicate: y >= ykK (TOPK) or every element
-    auto keep_k = [&](uint32_t yk) { return !topk_done || yk >= ykK; };
-    uint64_t myq = 0;
-    enumerate([&](uint32_t yk, uint32_t col, uint64_t q) { if (keep_k(yk)) myq += q; });
-    const uint64_t Qk = cons_sum_u64(myq, s, tid);
-    uint32_t tstar = 0, id_cut = 0xffffffffu;
-    bool pcut = false, partial = false;
-    if (p.use_p) {
-        const double Qn = Qn_override > 0.0 ? Qn_override : (double)Qk;
-        const double Pd = (double)p.top_p * Qn;
-        if ((double)Qk <= Pd) { *not_covered = true; return -1; }
-        const uint64_t Pt = (uint64_t)floor(Pd);
-        SelOut so = block_select<true, false>(
-            [&](auto&& f) { enumerate([&](uint32_t yk, uint32_t col, uint64_t q) { if (keep_k(yk)) f(yk, q); }); },
-            Pt, 32, s, tid);
-        if (!so.ok) { *not_covered = true; return -1; }
-        tstar = so.key;
-        pcut = true;
-        const uint64_t qt = so.n_at ? so.at / so.n_at : 0;
-        uint64_t m = so.n_at;
-        if (qt > 0) { const uint64_t mm = (Pt - so.before) / qt + 1; if (mm < m) m = mm; }
-        if (m < so.n_at) {
-            partial = true;
-            SelOut si = block_select<false, true>(
-                [&](auto&& f) { enumerate([&](uint32_t yk, uint32_t col, uint64_t q) { if (yk == tstar) f(col, 1); }); },
-                m - 1, P.id_bits, s, tid);
-            id_cut = si.key;
+struct Located {
+    bool ok;
+    bool in_buffer;    // the key's elements were collected into [n0, n1)
+    uint32_t key;      // y-key of the element
+    uint64_t before;   // region mass strictly above key
+    uint64_t at;       // mass at key (all elements of that key)
+    uint32_t n_at;
+    uint64_t total;    // region mass
+    uint32_t n0, n1;
+};
+
+template <int DT>
+__device__ Located locate(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g, int tid,
+                          uint32_t rlo, uint32_t rhi, float ylo, float yhi, uint64_t target, float My, float scale,
+                          uint32_t slot0) {
+    const int lane = tid & 31;
+    Located L;
+    L.ok = false; L.in_buffer = false; L.total = 0; L.n0 = slot0; L.n1 = slot0;
+    if (rlo > rhi) return L;
+    const float span = yhi - ylo;
+    const float inv = (span > 0.0f && span < INFINITY) ? (float)NB / span : 0.0f;
+    auto lbin = [&](float y) -> uint32_t {
+        if (!(y > ylo)) return 0u;
+        const float t = (y - ylo) * inv;
+        return t >= (float)(NB - 1) ? (uint32_t)(NB - 1) : (uint32_t)t;
+    };
+    uint32_t* cn = s.cnts;
+    unsigned long long* bn = s.bins;
+    // ---- level 0: linear bins ----
+    cn[tid] = 0u; bn[tid] = 0ull;
+    csync();
+    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+        const float y = ydiv(p, x);
+        const uint32_t k = fkey(y);
+        const bool v = valid && k >= rlo && k <= rhi;
+        agg_add<false>(cn, bn, v, lbin(y), v ? q_of(efast(y, My), scale) : 0ull, lane);
+    });
+    csync();
+    L.total = cons_sum_u64(bn[tid], s, tid);
+    if (L.total == 0) return L;
+    if (target >= L.total) target = L.total - 1;
+    if (tid < 32) warp0_scan_bins<true, false>(s, cn, bn, NB, target, 0, tid);
+    csync();
+    const SelSlot r0 = s.ctl->sel[0];
+    csync();
+    if (!r0.ok) return L;
+    const uint32_t b0 = r0.digit;
+    uint64_t before = r0.before;
+    uint32_t cnt = r0.nat;
+    const uint32_t room = slot0 < (uint32_t)CAND_CAP ? (uint32_t)CAND_CAP - slot0 : 0u;
+    // ---- refine by key digits while the crossing set does not fit ----
+    uint32_t prefix = 0u, pmask = 0u;
+    int pass = 1;
+    if (cnt > room) {
+        uint32_t kmn = 0xffffffffu, kmx = 0u;
+        for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+            const float y = ydiv(p, x);
+            const uint32_t k = fkey(y);
+            if (valid && k >= rlo && k <= rhi && lbin(y) == b0) { kmn = min(kmn, k); kmx = max(kmx, k); }
+        });
+        kmn = cons_min_u32(kmn, s, tid);
+        kmx = cons_max_u32(kmx, s, tid);
+        int rem = varying_bits(kmn, kmx);
+        pmask = rem >= 32 ? 0u : ~((1u << rem) - 1u);
+        prefix = kmn & pmask;
+        if (rem == 0) {
+            // every element of the crossing bin has one key; ids come from a row pass
+            L.ok = true; L.key = kmn; L.before = before; L.at = r0.at; L.n_at = cnt;
+            return L;
+        }
+        while (cnt > room && rem > 0) {
+            const int w = rem < 8 ? rem : 8;
+            const int shift = rem - w;
+            const uint32_t dmask = (1u << w) - 1u;
+            const int nb = 1 << w;
+            cn[tid] = 0u; bn[tid] = 0ull;
+            csync();
+            for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+                const float y = ydiv(p, x);
+                const uint32_t k = fkey(y);
+                const bool v = valid && k >= rlo && k <= rhi && lbin(y) == b0 && (k & pmask) == prefix;
+                agg_add<false>(cn, bn, v, (k >> shift) & dmask, v ? q_of(efast(y, My), scale) : 0ull, lane);
+            });
+            csync();
+            if (tid < 32) warp0_scan_bins<true, false>(s, cn, bn, nb, target - before, pass & 1, tid);
+            csync();
+            const SelSlot rr = s.ctl->sel[pass & 1];
+            csync();
+            ++pass;
+            if (!rr.ok) return L;
+            before += rr.before;
+            prefix |= rr.digit << shift;
+            pmask |= dmask << shift;
+            rem = shift;
+            cnt = rr.nat;
+            if (cnt > room && rem == 0) {
+                // every remaining element has this key; its ids are found with a row pass
+                L.ok = true; L.key = prefix; L.before = before; L.at = rr.at; L.n_at = cnt;
+                return L;
+            }
         }
     }
-    auto keep_f = [&](uint32_t yk, uint32_t col) {
-        if (!keep_k(yk)) return false;
-        if (!pcut) return true;
-        if (yk > tstar) return true;
-        if (yk < tstar) return false;
-        return !partial || col <= id_cut;
-    };
-    myq = 0;
-    enumerate([&](uint32_t yk, uint32_t col, uint64_t q) { if (keep_f(yk, col)) myq += q; });
-    const uint64_t Qf = cons_sum_u64(myq, s, tid);
-    if (Qf == 0) return -1;
-    uint64_t target = (uint64_t)floor((double)p.u * (double)Qf);
-    if (target >= Qf) target = Qf - 1;
-    SelOut sd = block_select<false, false>(
-        [&](auto&& f) { enumerate([&](uint32_t yk, uint32_t col, uint64_t q) { if (keep_f(yk, col)) f(col, q); }); },
-        target, P.id_bits, s, tid);
-    if (P.out_probs) {
-        float* pr = P.out_probs + (int64_t)r * P.vocab;
-        for (int c = tid; c < P.vocab; c += NCT) pr[c] = 0.0f;
-        csync();
-        const double inv = 1.0 / (double)Qf;
-        enumerate([&](uint32_t yk, uint32_t col, uint64_t q) {
-            if (keep_f(yk, col)) pr[col] = (float)((double)q * inv);
-        });
-        csync();
+    // ---- collect the crossing set ----
+    if (tid == 0) s.ctl->ncol = 0u;
+    csync();
+    uint32_t kmn = 0xffffffffu, kmx = 0u;
+    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+        const float y = ydiv(p, x);
+        const uint32_t k = fkey(y);
+        if (valid && k >= rlo && k <= rhi && lbin(y) == b0 && (k & pmask) == prefix) {
+            const uint32_t pos = slot0 + atomicAdd(&s.ctl->ncol, 1u);
+            if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = k; s.cid[pos] = (uint32_t)c; }
+            kmn = min(kmn, k); kmx = max(kmx, k);
+        }
+    });
+    kmn = cons_min_u32(kmn, s, tid);
+    kmx = cons_max_u32(kmx, s, tid);
+    const uint32_t n1 = min((uint32_t)CAND_CAP, slot0 + s.ctl->ncol);
+    csync();
+    const SelOut so = block_select<true, false>(
+        [&](auto&& f) {
+            for (uint32_t i0 = slot0; i0 < n1; i0 += NCT) {
+                const uint32_t i = i0 + tid;
+                const bool v = i < n1;
+                const uint32_t k = v ? s.ckey[i] : 0u;
+                f(v, k, v ? q_of(efast(funkey(k), My), scale) : 0ull);
+            }
+        },
+        target - before, kmn, varying_bits(kmn, kmx), s, tid);
+    L.ok = so.ok; L.in_buffer = true; L.key = so.key; L.before = before + so.before; L.at = so.at; L.n_at = so.n_at;
+    L.n0 = slot0; L.n1 = n1;
+    return L;
+}
+
+// j-th smallest column (0-based) among entries [i0, i1) with key k.
+__device__ __forceinline__ uint32_t jth_id(const KParams& P, const Smem& s, int tid, uint32_t i0, uint32_t i1,
+                                           uint32_t k, uint32_t n_at, uint64_t j) {
+    if (n_at <= 1 || j == 0) {
+        uint32_t best = 0xffffffffu;
+        for (uint32_t i = i0 + tid; i < i1; i += NCT) if (s.ckey[i] == k) best = min(best, s.cid[i]);
+        return cons_min_u32(best, s, tid);
     }
-    return sd.ok ? (int)sd.key : -1;
+    const SelOut si = block_select<false, true>(
+        [&](auto&& f) {
+            for (uint32_t b = i0; b < i1; b += NCT) {
+                const uint32_t i = b + tid;
+                const bool v = i < i1 && s.ckey[i] == k;
+                f(v, v ? s.cid[i] : 0u, 1ull);
+            }
+        },
+        j, 0u, P.id_bits, s, tid);
+    return si.key;
+}
+// j-th smallest column among the row's elements whose y-key is k (row pass).
+template <int DT>
+__device__ uint32_t jth_id_row(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g, int tid,
+                               uint32_t k, uint64_t j) {
+    const SelOut si = block_select<false, true>(
+        [&](auto&& f) {
+            for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+                const bool v = valid && fkey(ydiv(p, x)) == k;
+                f(v, (uint32_t)c, 1ull);
+            });
+        },
+        j, 0u, P.id_bits, s, tid);
+    return si.key;
 }
 
 // ---------------------------------------------------------------------------
-// Producer warp (one elected lane)
+// Producer warp (one elected lane): row queue + bulk copies into the ring
 // ---------------------------------------------------------------------------
 template <int DT>
 __device__ void producer(const KParams& P, const Smem& s) {
     constexpr int ESZ = Elem<DT>::SIZE;
-    constexpr int64_t TB = (int64_t)TILE_ELEMS * ESZ;
     volatile int* abort = &s.ctl->abort;
     const uint32_t ns = (uint32_t)P.nstage;
-    uint32_t it = 0;
-    for (int r = blockIdx.x; r < P.batch; r += gridDim.x) {
-        const RowGeom g = row_geom<ESZ>(P, r);
+    uint32_t it = 0, k = 0, st = 0, ph = 0;
+    auto fetch = [&]() -> int {
+        const unsigned v = atomicAdd(&P.ws->next_row, 1u);
+        return v < (unsigned)P.batch ? (int)v : -1;
+    };
+    auto drain = [&]() {
+        const uint32_t first = it > ns ? it - ns : 0u;
+        for (uint32_t j = first; j < it; ++j) mbar_wait_for(&s.full[j % ns], (j / ns) & 1u, WAIT_LIMIT_NS);
+    };
+    auto give_up = [&](int rr) {
+        *abort = 1;
+        if (rr >= 0) { P.out_ids[rr] = -1; if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT; }
+        drain();
+    };
+    int r = fetch();
+    while (true) {
+        const uint32_t slot = k % RQ, rph = (k / RQ) & 1u;
+        if (!mbar_wait(&s.rowempty[slot], rph ^ 1u, abort)) { give_up(r); return; }
+        s.ctl->rowq[slot] = r;
+        mbar_arrive(&s.rowfull[slot]);
+        ++k;
+        if (r < 0) return;
+        const int rcur = r;
+        r = fetch();  // next row index, fetched while this row streams
+        const RowGeom g = row_geom<ESZ>(P, rcur);
         for (int t = 0; t < g.ntiles; ++t, ++it) {
-            const uint32_t st = it % ns, ph = (it / ns) & 1u;
-            if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) {
-                *abort = 1;
-                // let copies already issued land before the block can exit
-                const uint32_t first = it > ns ? it - ns : 0u;
-                for (uint32_t j = first; j < it; ++j) {
-                    const uint64_t t0 = globaltimer_ns();
-                    while (!mbar_test(&s.full[j % ns], (j / ns) & 1u))
-                        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) break;
-                }
-                return;
-            }
-            const int64_t off = (int64_t)t * TB;
-            const uint32_t bytes = (uint32_t)((g.interior_bytes - off) < TB ? (g.interior_bytes - off) : TB);
+            if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) { give_up(r); return; }
+            const int64_t off = (int64_t)t * TILE_BYTES;
+            const int64_t left = g.interior_bytes - off;
+            const uint32_t bytes = (uint32_t)(left < TILE_BYTES ? left : TILE_BYTES);
             mbar_arrive_expect_tx(&s.full[st], bytes);
-            bulk_g2s(s.ring + (int64_t)st * TB, g.interior + off, bytes, &s.full[st]);
+            bulk_g2s(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st]);
+            if (++st == ns) { st = 0; ph ^= 1u; }
         }
     }
 }
 
 // ---------------------------------------------------------------------------
-// Consumer warps
+// Consumer warps: one row
 // ---------------------------------------------------------------------------
+struct RingPos { uint32_t st, ph; };
+
 template <int DT>
-__device__ void consumer(const KParams& P, const Smem& s, const int tid) {
+__device__ void sample_row(const KParams& P, const Smem& s, const int tid, const int r, RingPos& rp) {
     using E = Elem<DT>;
     constexpr int ESZ = E::SIZE, VEC = E::VEC;
-    constexpr int64_t TB = (int64_t)TILE_ELEMS * ESZ;
-    constexpr int CPT = (int)(TB / 16 / NCT);
     const int lane = tid & 31, warp = tid >> 5;
     RowCtl* ctl = s.ctl;
     volatile int* abort = &ctl->abort;
     const uint32_t ns = (uint32_t)P.nstage;
     const float scale = __uint_as_float((uint32_t)(127 + P.mass_shift) << 23);  // 2^S
-    uint32_t it = 0;
-    for (int r = blockIdx.x; r < P.batch; r += gridDim.x) {
-        const RowParams p = row_params(P, r);
-        const RowGeom g = row_geom<ESZ>(P, r);
-        if (tid == 0) {
-            ctl->n = 0; ctl->hikey = 0; ctl->xmin = -INFINITY;
-            ctl->cand_on = p.cand ? 1 : 0; ctl->status = p.bad; ctl->general = 0;
-        }
-        csync();
-        if (p.pen) history_prologue(P, s, p, r, tid);
-        Stream st;
-        st.tmax = -INFINITY; st.zm = -1e30f; st.zmc = st.zm * p.c; st.z = 0.0f;
-        st.xmin = -INFINITY; st.cand = p.cand;
-        const uint8_t* rowp = reinterpret_cast<const uint8_t*>(P.logits) + (int64_t)r * P.row_stride * ESZ;
-        // ragged head/tail columns (at most 2*(VEC-1)), one per lane of warp 0
-        if (warp == 0) {
-            const int nh = g.head, nt = P.vocab - g.tail0;
-            const bool valid = lane < nh + nt;
-            const int c = lane < nh ? lane : g.tail0 + (lane - nh);
-            float x[1] = {-INFINITY};
-            if (valid) {
-                x[0] = E::load(rowp, c);
-                if (p.pen && (hist_bits(s, P.nwords, c, 1) & 1u)) x[0] = penalize(p, s, c, x[0]);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<ESZ>(P, r);
+    if (tid == 0) {
+        ctl->wcnt[0] = ctl->wcnt[1] = ctl->wcnt[2] = 0u;
+        ctl->ovf[0] = ctl->ovf[1] = ctl->ovf[2] = 0;
+        ctl->hikey = 0u; ctl->lokey = 0xffffffffu; ctl->xmin = -INFINITY;
+        ctl->status = p.bad; ctl->nunique = 0u;
+    }
+    csync();
+    if (p.pen) history_prologue(P, s, p, r, tid);
+    const uint32_t U = p.pen ? ctl->nunique : 0u;
+    Stream st;
+    st.tmax = -INFINITY; st.imax = -INFINITY; st.itile = -1; st.tmin = INFINITY;
+    st.zm = -1e30f; st.nzmc = -(st.zm * p.c); st.z0 = 0.0f; st.z1 = 0.0f;
+    st.xmin = -INFINITY; st.cand = p.cand; st.base = 0; st.win = 0;
+    st.bestv = -INFINITY; st.bestc = 0xffffffffu;
+    const uint8_t* rowp = reinterpret_cast<const uint8_t*>(P.logits) + (int64_t)r * P.row_stride * ESZ;
+
+    // ---- ragged head/tail columns (at most 2 * (VEC - 1)), one per lane of warp 0 ----
+    if (warp == 0) {
+        const int nh = g.head, nt = P.vocab - g.tail0;
+        bool valid = lane < nh + nt;
+        const int c = lane < nh ? lane : g.tail0 + (lane - nh);
+        float x = -INFINITY;
+        if (valid) {
+            x = E::load(rowp, c);
+            if (p.pen && (hist_bits(s, P.nwords, c, 1) & 1u)) {
+                const uint32_t rk = hist_rank(s, (uint32_t)c);
+                if (rk < U) s.sval[rk] = x;   // merged after the stream
+                valid = false;
             }
-            process<1>(p, s, st, x, valid ? c : 0, valid ? 1u : 0u, lane);
         }
-        // streamed interior
-        for (int t = 0; t < g.ntiles; ++t, ++it) {
-            const uint32_t sidx = it % ns, ph = (it / ns) & 1u;
-            const bool ok = mbar_wait(&s.full[sidx], ph, abort);
-            if (!ok) *abort = 1;
-            const uint8_t* tile = s.ring + (int64_t)sidx * TB;
-            const int64_t rem = g.interior_bytes - (int64_t)t * TB;
-            const int nch = (int)((rem < TB ? rem : TB) / 16);
+        process_one(p, s, st, x, (uint32_t)(valid ? c : 0), valid, lane);
+    }
+
+    // ---- streamed interior ----
+    for (int t = 0; t < g.ntiles; ++t) {
+        const bool ok = mbar_wait(&s.full[rp.st], rp.ph, abort);
+        if (!ok) *abort = 1;
+        const uint8_t* tile = s.ring + (int64_t)rp.st * TILE_BYTES;
+        const int64_t left = g.interior_bytes - (int64_t)t * TILE_BYTES;
+        const int nch = ok ? (int)((left < TILE_BYTES ? left : TILE_BYTES) / 16) : 0;
+        const int tcol0 = g.head + t * (TILE_BYTES / ESZ);
+        uint4 v[CPT];
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+            const int ch = tid + j * NCT;
+            if (ch < nch) v[j] = *reinterpret_cast<const uint4*>(tile + ch * 16);
+            else v[j] = make_uint4(Neg<DT>::W, Neg<DT>::W, Neg<DT>::W, Neg<DT>::W);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[rp.st]);   // the stage now lives in registers
+        if (++rp.st == ns) { rp.st = 0; rp.ph ^= 1u; }
+        uint32_t hb[CPT];
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) hb[j] = 0u;
+        if (p.pen) {
 #pragma unroll
             for (int j = 0; j < CPT; ++j) {
                 const int ch = tid + j * NCT;
-                const bool valid = ok && ch < nch;
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (valid) v = *reinterpret_cast<const uint4*>(tile + (int64_t)ch * 16);
-                float x[VEC];
-                E::unpack(v, x);
-                const int c0 = g.head + (int)(((int64_t)t * TB + (int64_t)ch * 16) / ESZ);
-                if (valid && p.pen) penalize_chunk<VEC>(p, s, P.nwords, c0, x);
-                process<VEC>(p, s, st, x, c0, valid ? ((1u << VEC) - 1u) : 0u, lane);
+                if (ch < nch) {
+                    const int c0 = tcol0 + ch * VEC;
+                    uint32_t bits = hist_bits(s, P.nwords, c0, VEC);
+                    hb[j] = bits;
+                    while (bits) {
+                        const int e = __ffs(bits) - 1;
+                        bits &= bits - 1;
+                        const uint32_t rk = hist_rank(s, (uint32_t)(c0 + e));
+                        if (rk < U) s.sval[rk] = elem_get<DT>(v[j], e);
+                        elem_mask<DT>(v[j], e);
+                    }
+                }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.empty[sidx]);
-            if (((t + 1) % CHECK_TILES) == 0 || t == g.ntiles - 1) {
+        }
+        const float m = chunks_max<DT>(v);
+        st.tmax = fmax_nan(st.tmax, m);
+        if (p.mode == MODE_GREEDY && m > st.imax) { st.imax = m; st.itile = t; }
+        if (p.zsum) {
+            st.tmin = fminf(st.tmin, chunks_min<DT>(v));
+            if (m > st.zm) {
+                const float nn = -(m * p.c);
+                const float f = ex2_approx(nn - st.nzmc);
+                st.z0 *= f; st.z1 *= f;
+                st.zm = m; st.nzmc = nn;
+            }
+            chunks_sumexp<DT>(v, p.c, st.nzmc, st.z0, st.z1);
+        }
+        if (st.cand) {
+            if (t == 0) {
+                // starting threshold from the first tile: the K-th largest of
+                // disjoint group maxima (thread maxima for K <= NCT/2, chunk
+                // maxima for K <= NCT, elements otherwise) bounds the row's K-th
+                // largest from below
+                float cm[CPT];
+#pragma unroll
+                for (int j = 0; j < CPT; ++j) cm[j] = chunk_max1<DT>(v[j]);
+                const int K = p.K;
+                const SelOut so = block_select<true, true>(
+                    [&](auto&& f) {
+                        if (K <= NCT / 2) {
+                            f(m == m && m > -INFINITY, fkey(m), 1ull);
+                        } else if (K <= NCT) {
+#pragma unroll
+                            for (int j = 0; j < CPT; ++j) f(cm[j] == cm[j] && cm[j] > -INFINITY, fkey(cm[j]), 1ull);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < CPT; ++j)
+#pragma unroll
+                                for (int e = 0; e < VEC; ++e) {
+                                    const float x = elem_get<DT>(v[j], e);
+                                    f(x == x && x > -INFINITY, fkey(x), 1ull);
+                                }
+                        }
+                    },
+                    (uint64_t)(K - 1), 0u, 32, s, tid);
+                if (so.ok && tid == 0) {
+                    const float xm = xmin_for(p, funkey(so.key));
+                    if (xm > ctl->xmin) ctl->xmin = xm;
+                }
                 csync();
-                const uint32_t n = ctl->n;
-                const bool need = ctl->cand_on && n > (uint32_t)HWM;
-                csync();
-                if (need) compact(p, s, tid, n);
                 st.xmin = ctl->xmin;
-                st.cand = ctl->cand_on != 0;
             }
+            uint32_t pick = 0;
+            if (m >= st.xmin) {
+#pragma unroll
+                for (int j = 0; j < CPT; ++j) {
+                    const int ch = tid + j * NCT;
+                    if (ch < nch) {
+#pragma unroll
+                        for (int e = 0; e < VEC; ++e)
+                            if (!((hb[j] >> e) & 1u) && elem_get<DT>(v[j], e) >= st.xmin) pick |= 1u << (j * VEC + e);
+                    }
+                }
+            }
+            if (__any_sync(0xffffffffu, pick)) {
+                warp_append(s, st, pick, lane, [&](int i, uint32_t& key, uint32_t& col) {
+                    const int j = i / VEC, e = i % VEC;
+                    uint4 vv = v[0];
+#pragma unroll
+                    for (int jj = 1; jj < CPT; ++jj) if (jj == j) vv = v[jj];
+                    key = fkey(elem_get<DT>(vv, e));
+                    col = (uint32_t)(tcol0 + (tid + j * NCT) * VEC + e);
+                });
+            }
+            // appends per tile fall off as 1/t: check every tile early in the
+            // row, every 2nd and then every 4th tile later (appends are bounds
+            // checked, an overflow sends the row to the multi-pass path)
+            const bool chk = t < 8 || (t < 16 ? (t & 1) == 1 : (t & 3) == 3) || t == g.ntiles - 1;
+            if (chk) window_check(p, s, tid, st, (uint32_t)HWM);
         }
-        // uniform snapshot of the abort flag (the producer may set it at any time)
-        if (tid == 0) ctl->u32a = (*abort != 0) ? 1u : 0u;
+    }
+
+    // ---- merge the history columns with their penalised values ----
+    if (p.pen) {
         csync();
-        // ---- row statistics ----
-        const float M = cons_max_nan(st.tmax, s, tid);
-        int64_t out_id = -1;
-        int status = ctl->status;
-        const bool aborted = ctl->u32a != 0;
-        if (aborted) status |= FG_ROW_TIMEOUT;
-        double Zq = 0.0;
-        if (p.mode == MODE_NUCLEUS && !aborted) {
-            double zc = 0.0;
-            if (st.z > 0.0f)
-                zc = (double)st.z * exp2((double)st.zmc - (double)M * (double)p.c);
-            const double Zd = cons_sum_f64(zc, s, tid);
-            const float My = ydiv(p, M);
-            Zq = Zd * exp((double)M / (double)p.T - (double)My) * (double)scale;
+        for (uint32_t i0 = 0; i0 < U; i0 += NCT) {
+            const uint32_t i = i0 + tid;
+            const bool valid = i < U;
+            float x = -INFINITY;
+            uint32_t col = 0;
+            if (valid) { col = s.scol[i]; x = penalize(p, s, i, s.sval[i]); }
+            process_one(p, s, st, x, col, valid, lane);
         }
-        const bool cand_ok = ctl->cand_on != 0 && ctl->general == 0;
-        const uint32_t n = ctl->n;
-        csync();
-        if (aborted) {
-            // nothing trustworthy in this row
-        } else if (status & (FG_ROW_BAD_PARAM | FG_ROW_BAD_UNIFORM)) {
-            out_id = -1;
-        } else if (p.mode == MODE_GREEDY) {
-            status |= FG_ROW_GREEDY;
-            if (M != M) {
-                // torch.argmax: first NaN
-                uint32_t best = 0xffffffffu;
-                for_row<DT>(P, s, p, r, g, tid, [&](int c, float x) { if (x != x) best = min(best, (uint32_t)c); });
-                best = cons_min_u32(best, s, tid);
-                out_id = best;
-                status |= FG_ROW_GENERAL_PATH;
-            } else if (cand_ok) {
-                const uint32_t km = fkey(M);
-                uint32_t best = 0xffffffffu;
-                for (uint32_t i = tid; i < n; i += NCT) if (s.ckey[i] == km) best = min(best, s.cid[i]);
-                best = cons_min_u32(best, s, tid);
-                out_id = best;
-            } else {
-                uint32_t best = 0xffffffffu;
-                for_row<DT>(P, s, p, r, g, tid, [&](int c, float x) { if (x == M) best = min(best, (uint32_t)c); });
-                best = cons_min_u32(best, s, tid);
-                out_id = best;
-                status |= FG_ROW_GENERAL_PATH;
-            }
-            if (P.out_probs && out_id >= 0) {
-                float* pr = P.out_probs + (int64_t)r * P.vocab;
-                for (int c = tid; c < P.vocab; c += NCT) pr[c] = (c == (int)out_id) ? 1.0f : 0.0f;
-            }
-        } else if (M != M) {
-            status |= FG_ROW_NAN;
-        } else if (M == INFINITY) {
-            status |= FG_ROW_POS_INF;
-        } else if (M == -INFINITY) {
-            status |= FG_ROW_ALL_MASKED;
+    }
+    if (st.cand) window_check(p, s, tid, st, (uint32_t)HWM + (CAND_CAP - HWM) / 2);
+    // uniform snapshot of the abort flag (the producer may set it at any time)
+    if (tid == 0) ctl->snap = (*abort != 0) ? 1u : 0u;
+    csync();
+    const bool aborted = ctl->snap != 0;
+
+    // ---- row statistics ----
+    const float M = cons_max_nan(st.tmax, s, tid);
+    int status = ctl->status;
+    const bool cand_ok = st.cand && !aborted;
+    const uint32_t n = st.base;
+    double Zq = 0.0;
+    float My = M;
+    float ymin = -INFINITY;
+    if (p.zsum && !aborted && M == M && M > -INFINITY && M < INFINITY) {
+        My = ydiv(p, M);
+        double zc = 0.0;
+        const double zsum = (double)st.z0 + (double)st.z1;
+        if (zsum > 0.0) zc = zsum * exp2(-(double)st.nzmc - (double)M * (double)p.c);
+        const double Zd = cons_sum_f64(zc, s, tid);
+        Zq = Zd * exp((double)M / (double)p.T - (double)My) * (double)scale;
+        ymin = ydiv(p, cons_min_f(st.tmin, s, tid));
+    }
+    int64_t out_id = -1;
+    float* pr = P.out_probs ? P.out_probs + (int64_t)r * P.vocab : nullptr;
+
+    if (aborted) {
+        status |= FG_ROW_TIMEOUT;
+    } else if (status & (FG_ROW_BAD_PARAM | FG_ROW_BAD_UNIFORM)) {
+        out_id = -1;
+    } else if (p.mode == MODE_GREEDY) {
+        status |= FG_ROW_GREEDY;
+        uint32_t best = 0xffffffffu;
+        if (M != M) {
+            for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) { if (valid && x != x) best = min(best, (uint32_t)c); });
+            status |= FG_ROW_GENERAL_PATH;
         } else {
-            const float My = ydiv(p, M);
-            bool done = false;
-            if (cand_ok && p.mode != MODE_FULL) {
-                // candidates -> y-keys and masses
-                for (uint32_t i = tid; i < n; i += NCT) s.ckey[i] = fkey(ydiv(p, funkey(s.ckey[i])));
-                csync();
-                uint32_t ykK = 0;
-                bool topk = false;
-                if (p.mode == MODE_TOPK) {
-                    SelOut so = block_select<true, true>(
-                        [&](auto&& f) { for (uint32_t i = tid; i < n; i += NCT) f(s.ckey[i], 1ull); },
-                        (uint64_t)(p.K - 1), 32, s, tid);
-                    topk = true;
-                    ykK = so.ok ? so.key : 0u;
+            if (st.bestv == M) best = st.bestc;
+            if (st.imax == M && st.itile >= 0) {
+                // first column of this thread's chunks in that tile holding M
+                const int t = st.itile;
+                const int64_t left = g.interior_bytes - (int64_t)t * TILE_BYTES;
+                const int nch = (int)((left < TILE_BYTES ? left : TILE_BYTES) / 16);
+                const int tcol0 = g.head + t * (TILE_BYTES / ESZ);
+                for (int j = 0; j < CPT; ++j) {
+                    const int ch = tid + j * NCT;
+                    if (ch >= nch) break;
+                    const uint4 v = __ldg(reinterpret_cast<const uint4*>(g.interior + (int64_t)t * TILE_BYTES) + ch);
+                    const int c0 = tcol0 + ch * VEC;
+                    const uint32_t hbits = p.pen ? hist_bits(s, P.nwords, c0, VEC) : 0u;
+                    int found = -1;
+#pragma unroll
+                    for (int e = VEC - 1; e >= 0; --e)
+                        if (!((hbits >> e) & 1u) && elem_get<DT>(v, e) == M) found = e;
+                    if (found >= 0) { best = min(best, (uint32_t)(c0 + found)); break; }
                 }
-                for (uint32_t i = tid; i < n; i += NCT) {
-                    const uint32_t yk = s.ckey[i];
-                    s.q[i] = (!topk || yk >= ykK) ? mass_q(funkey(yk), My, scale) : 0ull;
-                }
-                csync();
-                bool not_cov = false;
-                const int j = decide(P, s, p, r, tid,
-                    [&](auto&& f) { for (uint32_t i = tid; i < n; i += NCT) f(s.ckey[i], s.cid[i], s.q[i]); },
-                    topk, ykK, p.mode == MODE_NUCLEUS ? Zq : -1.0, &not_cov);
-                if (!not_cov) { out_id = j; done = true; }
             }
-            if (!done) {
-                status |= FG_ROW_GENERAL_PATH;
-                auto row_enum = [&](auto&& f) {
-                    for_row<DT>(P, s, p, r, g, tid, [&](int c, float x) {
-                        const float y = ydiv(p, x);
-                        f(fkey(y), (uint32_t)c, mass_q(y, My, scale));
-                    });
-                };
-                uint32_t ykK = 0;
-                bool topk = false;
-                if (p.mode == MODE_TOPK) {
-                    SelOut so = block_select<true, true>(
-                        [&](auto&& f) { for_row<DT>(P, s, p, r, g, tid, [&](int c, float x) { f(fkey(ydiv(p, x)), 1ull); }); },
-                        (uint64_t)(p.K - 1), 32, s, tid);
-                    topk = true;
-                    ykK = so.ok ? so.key : 0u;
-                }
-                bool not_cov = false;
-                out_id = decide(P, s, p, r, tid, row_enum, topk, ykK, -1.0, &not_cov);
-            }
-            if (out_id < 0 && !(status & FG_ROW_ERROR_MASK)) status |= FG_ROW_ALL_MASKED;
         }
+        best = cons_min_u32(best, s, tid);
+        out_id = best;
+        if (pr) for (int c = tid; c < P.vocab; c += NCT) pr[c] = (c == (int)best) ? 1.0f : 0.0f;
+    } else if (M != M) {
+        status |= FG_ROW_NAN;
+    } else if (M == INFINITY) {
+        status |= FG_ROW_POS_INF;
+    } else if (M == -INFINITY) {
+        status |= FG_ROW_ALL_MASKED;
+    } else {
+        // ================= sampling rows =================
+        My = ydiv(p, M);
+        const uint32_t hiY = fkey(My);
+        if (ymin < My - 64.0f || !(ymin == ymin)) ymin = My - 64.0f;   // masses below are 0 at 2^-S
+        // candidate set C = {y >= y(xmin)} (complete); empty when the filter overflowed
+        uint32_t nC = cand_ok ? n : 0u;
+        const uint32_t loY = cand_ok ? fkey(ydiv(p, ctl->xmin)) : 0xffffffffu;
+        if (nC > 0) {
+            for (uint32_t i = tid; i < nC; i += NCT) s.ckey[i] = fkey(ydiv(p, funkey(s.ckey[i])));
+            csync();
+        }
+        const uint32_t cLo = min(loY, hiY);
+        const int remC = varying_bits(cLo, hiY);
+        auto qC = [&](uint32_t yk) { return q_of(expf(funkey(yk) - My), scale); };   // exact masses in C
+        // top-k threshold (on C, or over the whole row when C cannot hold it)
+        uint32_t ykK = 0u;
+        if (p.mode == MODE_TOPK) {
+            if (cand_ok) {
+                const SelOut so = block_select<true, true>(
+                    [&](auto&& f) {
+                        for (uint32_t i0 = 0; i0 < nC; i0 += NCT) {
+                            const uint32_t i = i0 + tid;
+                            f(i < nC, i < nC ? s.ckey[i] : 0u, 1ull);
+                        }
+                    },
+                    (uint64_t)(p.K - 1), cLo, remC, s, tid);
+                ykK = so.ok ? so.key : 0u;
+            } else {
+                const SelOut so = block_select<true, true>(
+                    [&](auto&& f) {
+                        for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+                            f(valid && x == x, fkey(ydiv(p, x)), 1ull);
+                        });
+                    },
+                    (uint64_t)(p.K - 1), 0u, 32, s, tid);
+                ykK = so.ok ? so.key : 0u;
+                nC = 0;
+            }
+        }
+        auto keepk = [&](uint32_t yk) { return p.mode != MODE_TOPK || yk >= ykK; };
+        uint64_t loc = 0;
+        for (uint32_t i = tid; i < nC; i += NCT) if (keepk(s.ckey[i])) loc += qC(s.ckey[i]);
+        const uint64_t AC = cons_sum_u64(loc, s, tid);   // exact mass of the kept part of C
+
+        // region R below C (whole row when C is empty), restricted to y >= T_K for top-k
+        const uint32_t rlo = (p.mode == MODE_TOPK) ? ykK : KEY_NEG_INF;
+        const uint32_t rhi = nC > 0 ? loY - 1u : 0xffffffffu;
+        const float yRlo = (p.mode == MODE_TOPK) ? fmaxf(funkey(ykK), My - 64.0f) : ymin;
+        const float yRhi = nC > 0 ? funkey(loY - 1u) : My;
+        bool cut = false, cut_in_R = false;
+        uint32_t tstar = 0u, id_cut = 0xffffffffu;
+        uint64_t Qf = 0, m_t = 0, n_t = 0;
+        if (p.use_p) {
+            double Qn;
+            if (p.mode == MODE_TOPK && cand_ok) Qn = (double)AC;
+            else if (p.mode == MODE_TOPK) {
+                const Located L0 = locate<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, 0ull, My, scale, 0u);
+                Qn = (double)L0.total;
+            } else Qn = Zq;
+            const double Pd = (double)p.top_p * Qn;
+            const uint64_t Pt = (uint64_t)floor(Pd);
+            cut = true;
+            if ((double)AC > Pd && nC > 0) {
+                const SelOut so = block_select<true, false>(
+                    [&](auto&& f) {
+                        for (uint32_t i0 = 0; i0 < nC; i0 += NCT) {
+                            const uint32_t i = i0 + tid;
+                            const uint32_t yk = i < nC ? s.ckey[i] : 0u;
+                            const bool v = i < nC && keepk(yk);
+                            f(v, yk, v ? qC(yk) : 0ull);
+                        }
+                    },
+                    Pt, cLo, remC, s, tid);
+                tstar = so.key;
+                const uint64_t qt = so.n_at ? so.at / so.n_at : 0;
+                m_t = so.n_at; n_t = so.n_at;
+                if (qt > 0) { const uint64_t mm = (Pt - so.before) / qt + 1; if (mm < m_t) m_t = mm; }
+                Qf = so.before + m_t * qt;
+            } else {
+                status |= FG_ROW_GENERAL_PATH;
+                const uint64_t tr = Pt >= AC ? Pt - AC : 0ull;
+                const Located L = locate<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, tr, My, scale, nC);
+                if (!L.ok || tr >= L.total) {
+                    cut = false;               // the cut lies below every element: keep all
+                    Qf = AC + L.total;
+                } else {
+                    cut_in_R = true;
+                    tstar = L.key;
+                    const uint64_t qt = L.n_at ? L.at / L.n_at : 0;
+                    m_t = L.n_at; n_t = L.n_at;
+                    if (qt > 0) { const uint64_t mm = (tr - L.before) / qt + 1; if (mm < m_t) m_t = mm; }
+                    Qf = AC + L.before + m_t * qt;
+                }
+            }
+        } else {
+            if (p.mode == MODE_TOPK && cand_ok) Qf = AC;
+            else if (p.mode == MODE_TOPK) {
+                const Located L0 = locate<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, 0ull, My, scale, 0u);
+                Qf = L0.total;
+            } else Qf = (uint64_t)Zq;   // unfiltered: every token kept
+        }
+        // ---- inverse-CDF draw in descending-probability order ----
+        if (Qf > 0) {
+            uint64_t target = (uint64_t)floor((double)p.u * (double)Qf);
+            if (target >= Qf) target = Qf - 1;
+            if (target < AC && nC > 0) {
+                const SelOut sd = block_select<true, false>(
+                    [&](auto&& f) {
+                        for (uint32_t i0 = 0; i0 < nC; i0 += NCT) {
+                            const uint32_t i = i0 + tid;
+                            const uint32_t yk = i < nC ? s.ckey[i] : 0u;
+                            const bool v = i < nC && keepk(yk) && (!cut || cut_in_R || yk >= tstar);
+                            f(v, yk, v ? qC(yk) : 0ull);
+                        }
+                    },
+                    target, cLo, remC, s, tid);
+                if (sd.ok) {
+                    const uint64_t qd = sd.n_at ? sd.at / sd.n_at : 0;
+                    uint64_t j = qd ? (target - sd.before) / qd : 0;
+                    if (j >= sd.n_at) j = sd.n_at ? sd.n_at - 1 : 0;
+                    out_id = jth_id(P, s, tid, 0u, nC, sd.key, sd.n_at, j);
+                }
+            } else {
+                status |= FG_ROW_GENERAL_PATH;
+                const uint64_t t2 = target - (nC > 0 ? AC : 0ull);
+                const uint32_t rlo2 = cut_in_R ? tstar : rlo;
+                const float ylo2 = cut_in_R ? fmaxf(funkey(tstar), My - 64.0f) : yRlo;
+                const Located L = locate<DT>(P, s, p, r, g, tid, rlo2, rhi, ylo2, yRhi, t2, My, scale, nC);
+                if (L.ok) {
+                    const uint64_t qd = L.n_at ? L.at / L.n_at : 0;
+                    uint64_t j = qd ? (t2 - L.before) / qd : 0;
+                    if (j >= L.n_at) j = L.n_at ? L.n_at - 1 : 0;
+                    out_id = L.in_buffer ? jth_id(P, s, tid, L.n0, L.n1, L.key, L.n_at, j)
+                                         : jth_id_row<DT>(P, s, p, r, g, tid, L.key, j);
+                }
+            }
+        }
+        if (out_id < 0 && !(status & FG_ROW_ERROR_MASK)) status |= FG_ROW_ALL_MASKED;
+        // ---- kept-set probabilities (debug / oracle mode) ----
+        if (pr && out_id >= 0) {
+            // ties at the cut: the first m_t by ascending id are kept
+            if (cut && m_t < n_t) {
+                if (cut_in_R) {
+                    id_cut = jth_id_row<DT>(P, s, p, r, g, tid, tstar, m_t - 1);
+                } else {
+                    const SelOut si = block_select<false, true>(
+                        [&](auto&& f) {
+                            for (uint32_t i0 = 0; i0 < nC; i0 += NCT) {
+                                const uint32_t i = i0 + tid;
+                                const bool v = i < nC && s.ckey[i] == tstar;
+                                f(v, v ? s.cid[i] : 0u, 1ull);
+                            }
+                        },
+                        m_t - 1, 0u, P.id_bits, s, tid);
+                    id_cut = si.key;
+                }
+            }
+            const double inv = 1.0 / (double)Qf;
+            auto kept = [&](uint32_t yk, uint32_t c) {
+                if (!keepk(yk)) return false;
+                if (!cut) return true;
+                if (yk > tstar) return true;
+                if (yk < tstar) return false;
+                return c <= id_cut;
+            };
+            for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+                if (!valid) return;
+                const float y = ydiv(p, x);
+                const uint32_t yk = fkey(y);
+                float val = 0.0f;
+                if (kept(yk, (uint32_t)c)) {
+                    const bool inC = nC > 0 && yk >= loY;
+                    const float e = inC ? expf(y - My) : efast(y, My);
+                    val = (float)((double)q_of(e, scale) * inv);
+                }
+                pr[c] = val;
+            });
+        }
+    }
+    if (pr && out_id < 0) for (int c = tid; c < P.vocab; c += NCT) pr[c] = 0.0f;
+    if (tid == 0) {
+        P.out_ids[r] = (out_id >= 0) ? out_id + P.vocab_offset : -1;
+        if (P.out_status) P.out_status[r] = status;
+    }
+    csync();
+    if (aborted && tid == 0) *abort = 1;
+}
+
+template <int DT>
+__device__ void consumer(const KParams& P, const Smem& s, const int tid) {
+    RowCtl* ctl = s.ctl;
+    volatile int* abort = &ctl->abort;
+    RingPos rp{0u, 0u};
+    uint32_t k = 0;
+    while (true) {
+        const uint32_t slot = k % RQ, ph = (k / RQ) & 1u;
         if (tid == 0) {
-            P.out_ids[r] = (out_id >= 0) ? out_id + P.vocab_offset : -1;
-            if (P.out_status) P.out_status[r] = status;
+            const bool ok = mbar_wait(&s.rowfull[slot], ph, abort);
+            ctl->snap = ok ? (uint32_t)ctl->rowq[slot] : 0xfffffffeu;
         }
         csync();
-        if (aborted) {
-            // the pipeline gave up: report every remaining row of this CTA and leave
-            if (tid == 0)
-                for (int rr = r + gridDim.x; rr < P.batch; rr += gridDim.x) {
-                    P.out_ids[rr] = -1;
-                    if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT;
-                }
-            break;
+        const int r = (int)ctl->snap;
+        csync();
+        if (tid == 0 && r != -2) mbar_arrive(&s.rowempty[slot]);
+        ++k;
+        if (r < 0) break;
+        sample_row<DT>(P, s, tid, r, rp);
+        if (tid == 0) ctl->snap = (*abort != 0) ? 1u : 0u;
+        csync();
+        const bool aborted = ctl->snap != 0;
+        csync();
+        if (aborted) break;
+    }
+    if (tid == 0 && *abort) {
+        // report the rows this CTA can no longer process: published ones, then the rest
+        for (;; ++k) {
+            const uint32_t slot = k % RQ, ph = (k / RQ) & 1u;
+            if (!mbar_wait_for(&s.rowfull[slot], ph, 10000000ull)) break;
+            const int rr = ctl->rowq[slot];
+            mbar_arrive(&s.rowempty[slot]);
+            if (rr < 0) break;
+            P.out_ids[rr] = -1;
+            if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT;
+        }
+        for (;;) {
+            const unsigned v = atomicAdd(&P.ws->next_row, 1u);
+            if (v >= (unsigned)P.batch) break;
+            P.out_ids[v] = -1;
+            if (P.out_status) P.out_status[v] = FG_ROW_TIMEOUT;
         }
     }
 }
 
 template <int DT>
-__global__ void __launch_bounds__(NTHREADS, 1) fg_sample_kernel(const KParams P) {
+__global__ void __launch_bounds__(NTHREADS, 2) fg_sample_kernel(const KParams P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, P);
     const int tid = threadIdx.x;
     if (tid == 0) {
         for (int i = 0; i < P.nstage; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], NCW); }
+        for (int i = 0; i < RQ; ++i) { mbar_init(&s.rowfull[i], 1); mbar_init(&s.rowempty[i], 1); }
         s.ctl->abort = 0;
         fence_mbar_init();
     }
@@ -556,12 +1160,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) fg_sample_kernel(const KParams P)
         return;
     }
     consumer<DT>(P, s, tid);
+    // the last CTA to finish leaves the workspace zeroed for the next launch
+    csync();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(&P.ws->done_ctas, 1u) == gridDim.x - 1) {
+            P.ws->next_row = 0u;
+            P.ws->done_ctas = 0u;
+            __threadfence();
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
 // Row argmax with torch.argmax semantics (first NaN, else first maximum).
 // ---------------------------------------------------------------------------
-struct ArgBest { float v; uint32_t i; };
 __device__ __forceinline__ bool arg_better(float a, uint32_t ia, float b, uint32_t ib) {
     const bool an = a != a, bn = b != b;
     if (an != bn) return an;

@@ -1,25 +1,20 @@
-// fg_sample_kernel.cuh — fused decode-step sampler for sm_100a.
+// fg_sample_kernel.cuh — layout, per-row parameters and block-level primitives
+// of the fused decode-step sampler (sm_100a).
 //
-// One persistent CTA per SM walks rows r = blockIdx.x, +gridDim.x, ...
-//   warp NCW (producer): streams each row's 16-byte-aligned interior from HBM
-//     into a shared-memory ring of TILE_BYTES stages with 1-D bulk async copies
-//     (cp.async.bulk, completion on mbarriers);
-//   warps 0..NCW-1 (consumers): per row
-//     1. history prologue: bitmap of history ids (+ word prefix and counts when
-//        a frequency penalty is set), all in shared memory;
-//     2. single pass over the row: penalties at history ids, NaN-propagating
-//        max, online sum-exp (rows whose top-p runs over the whole
-//        vocabulary), and a candidate filter x >= xmin that appends
-//        (key, column) pairs to a shared buffer; xmin is a running lower bound
-//        on the K-th largest value, raised by periodic compactions;
-//     3. epilogue over the candidates: exact top-k threshold, fixed-point
-//        masses, top-p cut (ties in ascending id order), inverse-CDF draw —
-//        all as block radix selects over integer histograms, so the result does
-//        not depend on thread scheduling;
-//     4. general path when the candidates cannot decide the row (nucleus
-//        deeper than the candidates, ties beyond capacity, top_k above the
-//        on-chip limit, NaN rows, no filter at all): the same selects run over
-//        the whole row re-read from global memory (L2-resident after step 2).
+// Kernel structure (fg_kernels.cuh):
+//   one persistent CTA per SM, rows handed out dynamically (global counter in
+//   the caller's workspace) by a producer warp that also streams each row's
+//   16-byte-aligned interior HBM -> shared memory with 1-D bulk async copies
+//   (cp.async.bulk, completion counted on mbarriers) into a ring of 16 KB tiles;
+//   NCW consumer warps per tile: history columns are masked out (their raw
+//   values captured for a later merge), packed NaN-propagating max over whole
+//   16-byte chunks, online sum-exp for rows whose top-p runs over the whole
+//   vocabulary, and a candidate filter x >= xmin that appends (key, column)
+//   pairs to a shared buffer; xmin is an exact lower bound of the K-th largest
+//   value, raised by compactions (block radix select) when the buffer fills.
+//   The epilogue decides the row on the candidates with integer (fixed-point)
+//   masses; rows the candidates cannot decide use histogram passes over the
+//   row re-read from L2.
 //
 // Reference semantics (FlashGen): flashgen/sampling/sampler.py:57-169,
 // csrc/runtime/pipeline.cpp:267-342.
@@ -29,20 +24,28 @@
 
 namespace fg {
 
-constexpr int NCW = 16;                 // consumer warps
+constexpr int NCW = 8;                  // consumer warps
 constexpr int NCT = NCW * 32;           // consumer threads
 constexpr int NTHREADS = NCT + 32;      // + one producer warp
-constexpr int TILE_ELEMS = 4096;        // elements per ring stage
-constexpr int CHECK_TILES = 2;          // tiles between compaction checks
-constexpr int CAND_CAP = 12288;         // candidate buffer entries
-constexpr int HWM = CAND_CAP - CHECK_TILES * TILE_ELEMS - 64;  // compaction trigger
-constexpr int K_FAST_MAX = 2048;        // largest top_k decided on the candidates
-constexpr int K_NUCLEUS = 2048;         // candidate target for top-p-only rows
-constexpr int Q_CAP = 4096;             // kept entries whose masses fit on chip
+constexpr int TILE_BYTES = 8192;        // one ring stage
+constexpr int CPT = TILE_BYTES / 16 / NCT;  // 16-byte chunks per consumer thread per tile (2)
+constexpr int CAND_CAP = 4096;          // candidate buffer entries
+constexpr int HWM = 3072;               // compaction trigger (candidates after a check)
+constexpr int K_FAST_MAX = 1536;        // largest top_k decided on the candidates
+constexpr int K_NUCLEUS = 1536;         // candidate target for top-p-only / unfiltered rows
+constexpr int NB = 256;                 // histogram bins (8-bit digits); NB == NCT
+constexpr int RQ = 4;                   // row-queue slots
 constexpr int BAR_CONS = 1;             // named barrier of the consumer warps
-constexpr int NBINS = 256;
 
 enum Mode : int { MODE_GREEDY = 0, MODE_TOPK = 1, MODE_NUCLEUS = 2, MODE_FULL = 3 };
+
+// Per-call workspace (caller-owned, zero before the first call; every launch
+// leaves it zero again).
+struct Workspace {
+    unsigned int next_row;
+    unsigned int done_ctas;
+    unsigned int pad[62];
+};
 
 struct KParams {
     const void* logits;
@@ -62,93 +65,92 @@ struct KParams {
     int64_t* out_ids;
     int32_t* out_status;
     float* out_probs;
+    Workspace* ws;
     // shared-memory layout (byte offsets into dynamic smem)
     int32_t nstage;
-    int32_t nwords;          // bitmap words
-    int32_t hu_cap;          // count-table entries (0: no frequency penalty)
-    int32_t off_bitmap, off_prefix, off_counts, off_ring;
-    int32_t pen_possible;    // history + some penalty array present
+    int32_t nwords;          // history bitmap words
+    int32_t hu_cap;          // unique-history capacity (0: no penalties possible)
+    int32_t off_bins, off_cnts, off_ckey, off_cid;
+    int32_t off_bitmap, off_prefix, off_counts, off_sval, off_scol, off_ring;
+    int32_t pen_possible;
     int32_t mass_shift;      // S: masses are round(e * 2^S)
     int32_t id_bits;         // bits needed for a column index
 };
 
+struct SelSlot {
+    int ok;
+    uint32_t digit, nat;
+    uint64_t before, at;
+};
+
 struct RowCtl {
-    uint32_t n;          // candidates
-    uint32_t hikey;      // max key appended
-    float xmin;          // candidate filter (x >= xmin)
-    int cand_on;
+    int rowq[RQ];
+    int abort;
     int status;
-    int general;         // row needs the general path
-    int abort;           // pipeline gave up (timeout)
-    // selection results / broadcast slots
-    uint32_t sel_digit;
-    int sel_ok;
-    uint64_t sel_before, sel_at;
-    uint32_t sel_nat;
-    uint32_t u32a, u32b;
-    float f32a;
-    double f64a;
+    int ovf[3];              // per-window overflow flags
+    uint32_t wcnt[3];        // per-window append counters
+    uint32_t hikey, lokey;   // key range of the candidate buffer
+    float xmin;
+    uint32_t nunique;        // unique history columns in this call's range
+    uint32_t snap;
+    uint32_t ncol;           // collected entries (multi-pass paths)
+    SelSlot sel[2];          // select results, alternating between passes
 };
 
 struct Smem {
     uint64_t* full;
     uint64_t* empty;
+    uint64_t* rowfull;
+    uint64_t* rowempty;
     RowCtl* ctl;
-    uint64_t* red64;     // [NCW]
-    float* redf;         // [NCW]
-    uint32_t* red32;     // [NCW]
-    double* redd;        // [NCW]
-    unsigned long long* bins;  // [NBINS]
-    uint32_t* cnts;      // [NBINS]
-    uint32_t* ckey;      // [CAND_CAP]
-    uint32_t* cid;       // [CAND_CAP]
-    uint64_t* q;         // [Q_CAP] (aliases ckey[Q_CAP..])
+    uint64_t* red64;
+    float* redf;
+    uint32_t* red32;
+    double* redd;
+    unsigned long long* bins;  // [2][NB]
+    uint32_t* cnts;            // [2][NB]
+    uint32_t* ckey;            // [CAND_CAP]
+    uint32_t* cid;             // [CAND_CAP]
     uint32_t* bitmap;
-    uint32_t* prefix;
+    uint16_t* prefix;          // popcount of the bitmap before each 64-column pair of words
     uint32_t* counts;
+    float* sval;
+    uint32_t* scol;
     uint8_t* ring;
 };
 
 __host__ __device__ inline int align_up_i(int x, int a) { return (x + a - 1) / a * a; }
 
-// Fixed part of the layout (everything except bars, penalty tables and ring).
-struct FixedLayout {
-    int ctl, red64, redf, red32, redd, bins, cnts, ckey, cid, end;
-};
-__host__ __device__ inline FixedLayout fixed_layout(int nstage) {
-    FixedLayout L;
-    int o = 16 * nstage;  // full[nstage] + empty[nstage]
-    o = align_up_i(o, 16); L.ctl = o; o += (int)sizeof(RowCtl);
-    o = align_up_i(o, 16); L.red64 = o; o += 8 * NCW;
-    L.redf = o; o += 4 * NCW;
-    L.red32 = o; o += 4 * NCW;
-    o = align_up_i(o, 8); L.redd = o; o += 8 * NCW;
-    o = align_up_i(o, 16); L.bins = o; o += 8 * NBINS;
-    L.cnts = o; o += 4 * NBINS;
-    o = align_up_i(o, 16); L.ckey = o; o += 4 * CAND_CAP;
-    L.cid = o; o += 4 * CAND_CAP;
-    L.end = o;
-    return L;
+// Barriers + control block + reduction scratch; returns the first free offset.
+__host__ __device__ inline int head_bytes(int nstage) {
+    int o = 8 * (2 * nstage + 2 * RQ);
+    o = align_up_i(o, 16) + (int)sizeof(RowCtl);
+    o = align_up_i(o, 16) + (8 + 4 + 4 + 8) * NCW;
+    return align_up_i(o, 128);
 }
 
 __device__ __forceinline__ Smem carve(uint8_t* base, const KParams& P) {
-    FixedLayout L = fixed_layout(P.nstage);
     Smem s;
     s.full = reinterpret_cast<uint64_t*>(base);
     s.empty = s.full + P.nstage;
-    s.ctl = reinterpret_cast<RowCtl*>(base + L.ctl);
-    s.red64 = reinterpret_cast<uint64_t*>(base + L.red64);
-    s.redf = reinterpret_cast<float*>(base + L.redf);
-    s.red32 = reinterpret_cast<uint32_t*>(base + L.red32);
-    s.redd = reinterpret_cast<double*>(base + L.redd);
-    s.bins = reinterpret_cast<unsigned long long*>(base + L.bins);
-    s.cnts = reinterpret_cast<uint32_t*>(base + L.cnts);
-    s.ckey = reinterpret_cast<uint32_t*>(base + L.ckey);
-    s.cid = reinterpret_cast<uint32_t*>(base + L.cid);
-    s.q = reinterpret_cast<uint64_t*>(base + L.ckey + 4 * Q_CAP);
+    s.rowfull = s.empty + P.nstage;
+    s.rowempty = s.rowfull + RQ;
+    int o = align_up_i(8 * (2 * P.nstage + 2 * RQ), 16);
+    s.ctl = reinterpret_cast<RowCtl*>(base + o);
+    o = align_up_i(o + (int)sizeof(RowCtl), 16);
+    s.red64 = reinterpret_cast<uint64_t*>(base + o); o += 8 * NCW;
+    s.redd = reinterpret_cast<double*>(base + o); o += 8 * NCW;
+    s.redf = reinterpret_cast<float*>(base + o); o += 4 * NCW;
+    s.red32 = reinterpret_cast<uint32_t*>(base + o);
+    s.bins = reinterpret_cast<unsigned long long*>(base + P.off_bins);
+    s.cnts = reinterpret_cast<uint32_t*>(base + P.off_cnts);
+    s.ckey = reinterpret_cast<uint32_t*>(base + P.off_ckey);
+    s.cid = reinterpret_cast<uint32_t*>(base + P.off_cid);
     s.bitmap = reinterpret_cast<uint32_t*>(base + P.off_bitmap);
-    s.prefix = reinterpret_cast<uint32_t*>(base + P.off_prefix);
+    s.prefix = reinterpret_cast<uint16_t*>(base + P.off_prefix);
     s.counts = reinterpret_cast<uint32_t*>(base + P.off_counts);
+    s.sval = reinterpret_cast<float*>(base + P.off_sval);
+    s.scol = reinterpret_cast<uint32_t*>(base + P.off_scol);
     s.ring = base + P.off_ring;
     return s;
 }
@@ -167,8 +169,8 @@ __device__ __forceinline__ RowGeom row_geom(const KParams& P, int r) {
     RowGeom g;
     const uint8_t* start = reinterpret_cast<const uint8_t*>(P.logits) + (int64_t)r * P.row_stride * ESZ;
     const uint8_t* end = start + (int64_t)P.vocab * ESZ;
-    uintptr_t a0 = (reinterpret_cast<uintptr_t>(start) + 15) & ~uintptr_t(15);
-    uintptr_t a1 = reinterpret_cast<uintptr_t>(end) & ~uintptr_t(15);
+    const uintptr_t a0 = (reinterpret_cast<uintptr_t>(start) + 15) & ~uintptr_t(15);
+    const uintptr_t a1 = reinterpret_cast<uintptr_t>(end) & ~uintptr_t(15);
     if (a1 <= a0) {
         g.interior = start; g.interior_bytes = 0; g.head = P.vocab; g.tail0 = P.vocab; g.ntiles = 0;
         return g;
@@ -177,8 +179,7 @@ __device__ __forceinline__ RowGeom row_geom(const KParams& P, int r) {
     g.interior_bytes = (int64_t)(a1 - a0);
     g.head = (int)((a0 - reinterpret_cast<uintptr_t>(start)) / ESZ);
     g.tail0 = g.head + (int)(g.interior_bytes / ESZ);
-    constexpr int64_t TB = (int64_t)TILE_ELEMS * ESZ;
-    g.ntiles = (int)((g.interior_bytes + TB - 1) / TB);
+    g.ntiles = (int)((g.interior_bytes + TILE_BYTES - 1) / TILE_BYTES);
     return g;
 }
 
@@ -187,11 +188,12 @@ __device__ __forceinline__ RowGeom row_geom(const KParams& P, int r) {
 // ---------------------------------------------------------------------------
 struct RowParams {
     int mode;
-    int K;           // top-k (TOPK), candidate target otherwise
+    int K;           // top-k (TOPK) or candidate target
     bool use_p;
     bool cand;       // candidate filter requested
     bool pen, freq_on, pres_on, rep_on;
     bool temp_on;    // y = x / T
+    bool zsum;       // online sum-exp needed (NUCLEUS / FULL)
     float T, rT, top_p, rep, pres, freq, u;
     float c;         // log2(e) / T for the online sum-exp
     int bad;         // FG_ROW_BAD_PARAM / FG_ROW_BAD_UNIFORM
@@ -201,22 +203,22 @@ __device__ __forceinline__ RowParams row_params(const KParams& P, int r) {
     RowParams p;
     p.T = __ldg(P.temperature + r);
     p.top_p = __ldg(P.top_p + r);
-    int tk = __ldg(P.top_k + r);
+    const int tk = __ldg(P.top_k + r);
     p.rep = P.rep ? __ldg(P.rep + r) : 1.0f;
     p.pres = P.pres ? __ldg(P.pres + r) : 0.0f;
     p.freq = P.freq ? __ldg(P.freq + r) : 0.0f;
-    bool g = P.greedy ? (__ldg(P.greedy + r) != 0) : false;
+    const bool g = P.greedy ? (__ldg(P.greedy + r) != 0) : false;
     p.u = __ldg(P.uniforms + r);
     p.bad = 0;
-    bool hist = P.pen_possible && P.hist_offsets != nullptr &&
-                (__ldg(P.hist_offsets + r + 1) > __ldg(P.hist_offsets + r));
+    const bool hist = P.pen_possible && (__ldg(P.hist_offsets + r + 1) > __ldg(P.hist_offsets + r));
     p.rep_on = hist && (p.rep != 1.0f);
-    p.freq_on = hist && (p.freq != 0.0f) && P.hu_cap > 0;
+    p.freq_on = hist && (p.freq != 0.0f);
     p.pres_on = hist && (p.pres != 0.0f);
     p.pen = p.rep_on || p.freq_on || p.pres_on;
     if (!(p.rep == p.rep) || !(p.pres == p.pres) || !(p.freq == p.freq)) p.bad |= FG_ROW_BAD_PARAM;
+    p.zsum = false;
     if (g || p.T == 0.0f) {
-        p.mode = MODE_GREEDY; p.K = 1; p.use_p = false; p.cand = true; p.temp_on = false;
+        p.mode = MODE_GREEDY; p.K = 1; p.use_p = false; p.cand = false; p.temp_on = false;
         p.rT = 1.0f; p.c = 1.4426950408889634f;
         return p;
     }
@@ -230,10 +232,9 @@ __device__ __forceinline__ RowParams row_params(const KParams& P, int r) {
         p.mode = MODE_TOPK;
         p.K = tk < P.vocab ? tk : P.vocab;
         p.cand = (p.K <= K_FAST_MAX);
-    } else if (p.use_p) {
-        p.mode = MODE_NUCLEUS; p.K = K_NUCLEUS; p.cand = true;
     } else {
-        p.mode = MODE_FULL; p.K = 0; p.cand = false;
+        p.mode = p.use_p ? MODE_NUCLEUS : MODE_FULL;
+        p.K = K_NUCLEUS; p.cand = true; p.zsum = true;
     }
     return p;
 }
@@ -249,16 +250,13 @@ __device__ float xmin_for(const RowParams& p, float tau) {
     if (!p.temp_on || !(tau > -INFINITY)) return tau;
     const float yt = ydiv(p, tau);
     uint32_t k = fkey(tau);
-    int steps = 0;
-    while (k > KEY_NEG_INF && steps < 8) {
-        float xp = funkey(k - 1);
-        if (ydiv(p, xp) >= yt) { --k; ++steps; } else return funkey(k);
+    for (int steps = 0; steps < 8; ++steps) {
+        if (k <= KEY_NEG_INF) return funkey(k);
+        if (ydiv(p, funkey(k - 1)) >= yt) --k; else return funkey(k);
     }
-    if (k <= KEY_NEG_INF) return funkey(k);
-    // long run of x values with the same quotient: binary search below k
-    uint32_t lo = KEY_NEG_INF, hi = k;   // pred(hi) true; find smallest true
+    uint32_t lo = KEY_NEG_INF, hi = k;   // pred(hi) holds; smallest key where it holds
     while (lo < hi) {
-        uint32_t mid = lo + (hi - lo) / 2;
+        const uint32_t mid = lo + (hi - lo) / 2;
         if (ydiv(p, funkey(mid)) >= yt) hi = mid; else lo = mid + 1;
     }
     return funkey(hi);
@@ -277,6 +275,17 @@ __device__ __forceinline__ float cons_max_nan(float v, const Smem& s, int tid) {
     float r = s.redf[0];
 #pragma unroll
     for (int w = 1; w < NCW; ++w) r = fmax_nan(r, s.redf[w]);
+    csync();
+    return r;
+}
+__device__ __forceinline__ float cons_min_f(float v, const Smem& s, int tid) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((tid & 31) == 0) s.redf[tid >> 5] = v;
+    csync();
+    float r = s.redf[0];
+#pragma unroll
+    for (int w = 1; w < NCW; ++w) r = fminf(r, s.redf[w]);
     csync();
     return r;
 }
@@ -323,16 +332,16 @@ __device__ __forceinline__ double cons_sum_f64(double v, const Smem& s, int tid)
     csync();
     return r;
 }
-// Exclusive prefix over consumer threads (thread order), returns (excl, total).
+// Exclusive prefix over consumer threads in thread order; returns excl, sets total.
 __device__ __forceinline__ uint32_t cons_excl_scan_u32(uint32_t v, uint32_t& total, const Smem& s, int tid) {
     const int lane = tid & 31, w = tid >> 5;
-    uint32_t incl = warp_incl_scan_u32(v, lane);
+    const uint32_t incl = warp_incl_scan_u32(v, lane);
     if (lane == 31) s.red32[w] = incl;
     csync();
     uint32_t base = 0, tot = 0;
 #pragma unroll
     for (int i = 0; i < NCW; ++i) {
-        uint32_t t = s.red32[i];
+        const uint32_t t = s.red32[i];
         if (i < w) base += t;
         tot += t;
     }
@@ -342,15 +351,51 @@ __device__ __forceinline__ uint32_t cons_excl_scan_u32(uint32_t v, uint32_t& tot
 }
 
 // ---------------------------------------------------------------------------
-// Block radix select.
+// Warp-aggregated histogram add. Every lane of the warp calls it (valid says
+// whether the lane contributes). Lanes with the same digit are grouped with
+// match.any: the group leader adds the group's count, and the group's 64-bit
+// weight sum (three exact 21-bit partial sums), so no bin sees more than one
+// atomic per warp instruction.
+// ---------------------------------------------------------------------------
+template <bool COUNT>
+__device__ __forceinline__ void agg_add(uint32_t* cnts, unsigned long long* bins, bool valid, uint32_t d, uint64_t w,
+                                        int lane) {
+    const uint32_t vm = __ballot_sync(0xffffffffu, valid);
+    if (vm == 0u) return;
+    const uint32_t key = valid ? d : (0x80000000u | (uint32_t)lane);
+    const uint32_t peers = __match_any_sync(0xffffffffu, key) & vm;
+    const bool leader = valid && lane == __ffs(peers) - 1;
+    if (leader) atomicAdd(&cnts[d], (uint32_t)__popc(peers));
+    if (COUNT) return;
+    const bool solo = __popc(peers) == 1;
+    if (valid && solo && w) atomicAdd(&bins[d], (unsigned long long)w);
+    uint32_t todo = __ballot_sync(0xffffffffu, leader && !solo);
+    while (todo) {
+        const int ldr = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const uint32_t grp = __shfl_sync(0xffffffffu, peers, ldr);
+        const uint64_t part = ((grp >> lane) & 1u) ? w : 0ull;
+        const uint32_t s0 = __reduce_add_sync(0xffffffffu, (uint32_t)(part & 0x1fffffu));
+        const uint32_t s1 = __reduce_add_sync(0xffffffffu, (uint32_t)((part >> 21) & 0x1fffffu));
+        const uint32_t s2 = __reduce_add_sync(0xffffffffu, (uint32_t)(part >> 42));
+        if (lane == ldr) {
+            const uint64_t tot = (uint64_t)s0 + ((uint64_t)s1 << 21) + ((uint64_t)s2 << 42);
+            if (tot) atomicAdd(&bins[d], (unsigned long long)tot);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Block radix select with 8-bit digits.
 //
-// Over the multiset of (key, weight) pairs that `enumerate` yields in this
-// thread (every consumer thread yields its own share), find the key k* such
-// that  W(before k*) <= target < W(before k*) + W(at k*), where "before" means
-// larger keys (DESC) or smaller keys (ASC). Weights are summed exactly in
-// integers, so the answer does not depend on thread scheduling. COUNT selects
-// use weight 1 (the caller's weight argument is ignored).
-// Returns ok=false when target >= total weight.
+// Over the (key, weight) pairs every consumer thread yields through
+// `enumerate` — enumerate(f) calls f(valid, key, weight) the same number of
+// times in every lane of a warp — find key k* with
+//     W(before k*) <= target < W(before k*) + W(at k*),
+// "before" meaning larger keys (DESC) or smaller keys (ASC). Keys are known to
+// share their top (32 - rem) bits with `prefix`. Weights are summed exactly in
+// integers, so the result does not depend on thread scheduling. COUNT selects
+// ignore the weight and count elements. ok=false when target >= total.
 // ---------------------------------------------------------------------------
 struct SelOut {
     uint32_t key;
@@ -360,74 +405,112 @@ struct SelOut {
     bool ok;
 };
 
+// Number of low bits that vary among keys in [lo, hi].
+__device__ __forceinline__ int varying_bits(uint32_t lo, uint32_t hi) {
+    const uint32_t d = lo ^ hi;
+    return d == 0 ? 0 : 32 - __clz(d);
+}
+
+// Block-wide inclusive scan over the NCT threads (thread order).
+__device__ __forceinline__ uint64_t block_incl_scan_u64(uint64_t v, const Smem& s, int tid) {
+    const int lane = tid & 31, wid = tid >> 5;
+    uint64_t incl = warp_incl_scan_u64(v, lane);
+    if (lane == 31) s.red64[wid] = incl;
+    csync();
+    uint64_t base = 0;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) if (i < wid) base += s.red64[i];
+    return incl + base;
+}
+
+// Warp 0 scans the nb-bin histogram (nb <= NB) in (DESC ? descending :
+// ascending) digit order and writes, to sel[slot], the digit whose bin holds
+// `rel` (ok = 0 when rel >= total). Lane l owns scan positions [8l, 8l + 8).
+template <bool DESC, bool COUNT>
+__device__ __forceinline__ void warp0_scan_bins(const Smem& s, const uint32_t* cn, const unsigned long long* bn,
+                                                int nb, uint64_t rel, int slot, int lane) {
+    uint64_t v[8];
+    uint64_t lsum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int o = lane * 8 + j;
+        const int d = DESC ? nb - 1 - o : o;
+        v[j] = (o < nb) ? (COUNT ? (uint64_t)cn[d] : (uint64_t)bn[d]) : 0ull;
+        lsum += v[j];
+    }
+    const uint64_t incl = warp_incl_scan_u64(lsum, lane);
+    const uint64_t excl = incl - lsum;
+    const bool mine = (excl <= rel) && (rel < incl);
+    const uint32_t bal = __ballot_sync(0xffffffffu, mine);
+    SelSlot& o = s.ctl->sel[slot];
+    if (bal == 0) {
+        if (lane == 0) o.ok = 0;
+    } else if (lane == __ffs(bal) - 1) {
+        uint64_t c = excl;
+        int jj = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (jj == j && rel >= c + v[j]) { c += v[j]; jj = j + 1; }
+        }
+        if (jj > 7) jj = 7;
+        const int d = DESC ? nb - 1 - (lane * 8 + jj) : lane * 8 + jj;
+        o.ok = 1; o.digit = (uint32_t)d; o.before = c; o.nat = cn[d];
+        o.at = COUNT ? (uint64_t)cn[d] : (uint64_t)bn[d];
+    }
+}
+
 template <bool DESC, bool COUNT, class Enum>
-__device__ SelOut block_select(Enum&& enumerate, uint64_t target, int key_bits, const Smem& s, int tid) {
+__device__ SelOut block_select(Enum&& enumerate, uint64_t target, uint32_t prefix, int rem, const Smem& s,
+                               int tid) {
+    const int lane = tid & 31;
     SelOut out;
-    uint32_t prefix = 0, pmask = 0;
-    uint64_t before = 0;
-    int rem = key_bits;
+    uint32_t pmask = rem >= 32 ? 0u : ~((1u << rem) - 1u);
+    prefix &= pmask;
+    if (rem == 0) {
+        uint64_t wsum = 0, csum = 0;
+        enumerate([&](bool valid, uint32_t k, uint64_t wt) {
+            if (valid && k == prefix) { ++csum; if (!COUNT) wsum += wt; }
+        });
+        const uint64_t nat = cons_sum_u64(csum, s, tid);
+        const uint64_t W = COUNT ? nat : cons_sum_u64(wsum, s, tid);
+        out.key = prefix; out.before = 0; out.at = W; out.n_at = (uint32_t)nat; out.ok = target < W;
+        return out;
+    }
+    uint64_t before = 0, at = 0;
+    uint32_t nat = 0;
     bool ok = true;
-    uint64_t at = 0; uint32_t nat = 0;
+    int buf = 0, pass = 0;
+    s.cnts[tid] = 0u;
+    if (!COUNT) s.bins[tid] = 0ull;
+    csync();
     while (rem > 0) {
         const int w = rem < 8 ? rem : 8;
         const int shift = rem - w;
         const uint32_t dmask = (1u << w) - 1u;
-        if (tid < NBINS) { s.cnts[tid] = 0; if (!COUNT) s.bins[tid] = 0ull; }
-        csync();
-        enumerate([&](uint32_t k, uint64_t wt) {
-            if ((k & pmask) == prefix) {
-                uint32_t d = (k >> shift) & dmask;
-                atomicAdd(&s.cnts[d], 1u);
-                if (!COUNT) atomicAdd(&s.bins[d], (unsigned long long)wt);
-            }
+        uint32_t* cn = s.cnts + buf * NB;
+        unsigned long long* bn = s.bins + buf * NB;
+        // clear the other buffer for the next pass (it was last read before the
+        // previous pass's second barrier)
+        s.cnts[(buf ^ 1) * NB + tid] = 0u;
+        if (!COUNT) s.bins[(buf ^ 1) * NB + tid] = 0ull;
+        enumerate([&](bool valid, uint32_t k, uint64_t wt) {
+            const bool v = valid && ((k & pmask) == prefix);
+            agg_add<COUNT>(cn, bn, v, (k >> shift) & dmask, wt, lane);
         });
         csync();
-        if (tid < 32) {
-            const int lane = tid;
-            // lane covers 8 consecutive bins in scan order
-            uint64_t v[8];
-            uint64_t lsum = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                int o = lane * 8 + j;
-                int d = DESC ? (NBINS - 1 - o) : o;
-                uint64_t x = COUNT ? (uint64_t)s.cnts[d] : (uint64_t)s.bins[d];
-                v[j] = x; lsum += x;
-            }
-            uint64_t incl = warp_incl_scan_u64(lsum, lane);
-            uint64_t excl = incl - lsum;
-            uint64_t rel = target - before;  // target >= before by construction
-            bool mine = (excl <= rel) && (rel < incl);
-            uint32_t bal = __ballot_sync(0xffffffffu, mine);
-            if (bal == 0) {
-                if (lane == 0) { s.ctl->sel_ok = 0; s.ctl->sel_digit = 0; s.ctl->sel_before = 0; }
-            } else if (lane == __ffs(bal) - 1) {
-                uint64_t c = excl;
-                int jj = 0;
-                for (; jj < 7; ++jj) {
-                    if (rel < c + v[jj]) break;
-                    c += v[jj];
-                }
-                int o = lane * 8 + jj;
-                int d = DESC ? (NBINS - 1 - o) : o;
-                s.ctl->sel_ok = 1;
-                s.ctl->sel_digit = (uint32_t)d;
-                s.ctl->sel_before = c;
-            }
-        }
+        if (tid < 32) warp0_scan_bins<DESC, COUNT>(s, cn, bn, 1 << w, target - before, pass & 1, lane);
         csync();
-        if (!s.ctl->sel_ok) { ok = false; }
-        const uint32_t d = s.ctl->sel_digit;
-        before += s.ctl->sel_before;
-        nat = s.cnts[d];
-        at = COUNT ? (uint64_t)nat : (uint64_t)s.bins[d];
-        csync();
-        if (!ok) break;
-        prefix |= d << shift;
+        const SelSlot r = s.ctl->sel[pass & 1];
+        if (!r.ok) { ok = false; break; }
+        before += r.before;
+        nat = r.nat; at = r.at;
+        prefix |= r.digit << shift;
         pmask |= dmask << shift;
         rem = shift;
+        buf ^= 1; ++pass;
     }
     out.key = prefix; out.before = before; out.at = at; out.n_at = nat; out.ok = ok;
+    csync();   // every thread has read the last result slot before the next select writes it
     return out;
 }
 

@@ -85,11 +85,26 @@ class PackedParams:
                             [bool(p.greedy) for p in params], device)
 
 
+_WORKSPACES = {}
+
+
+def workspace_for(device: torch.device, stream: torch.cuda.Stream) -> torch.Tensor:
+    """The zero-initialised fg_sample workspace of (device, stream). Calls on one
+    stream are serialised by the stream, so they can share it."""
+    key = (device.index, stream.cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        ws = torch.zeros(_lib.FG_SAMPLE_WORKSPACE_BYTES // 4, dtype=torch.int32, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def fused_sample(logits: torch.Tensor, packed: PackedParams, uniforms: torch.Tensor,
                  hist: Optional[Tuple[torch.Tensor, torch.Tensor, int]] = None,
                  out: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None,
                  probs: Optional[torch.Tensor] = None, vocab_offset: int = 0, vocab_total: int = 0,
-                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+                 stream: Optional[torch.cuda.Stream] = None,
+                 workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One fg_sample call on device tensors (no checks beyond the C ABI's)."""
     lib = _lib.load()
     B, V = logits.shape
@@ -114,6 +129,9 @@ def fused_sample(logits: torch.Tensor, packed: PackedParams, uniforms: torch.Ten
     a.out_status = _ptr(status)
     a.out_probs = _ptr(probs)
     st = stream if stream is not None else torch.cuda.current_stream(logits.device)
+    if workspace is None:
+        workspace = workspace_for(logits.device, st)
+    a.workspace = workspace.data_ptr()
     with torch.cuda.device(logits.device):
         _lib.check(lib.fg_sample(a, st.cuda_stream), "fg_sample")
     return out

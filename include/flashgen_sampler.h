@@ -89,7 +89,7 @@ extern "C" {
  * hist_offsets[r+1]). Ids are global vocabulary ids in [0, vocab_total);
  * repeats are allowed (they are the frequency counts). Both pointers NULL
  * means no history. `hist_max_len` must bound every row's history length (it
- * sizes the on-chip count table; only used when a frequency penalty is set).
+ * sizes the on-chip history tables; at most 65535 unique ids per row).
  *
  * Vocabulary sharding: `vocab_offset` is the global id of column 0 and
  * `vocab_total` the full vocabulary size (0 means vocab_total = vocab). Output
@@ -118,7 +118,17 @@ typedef struct FgSampleArgs {
     int32_t*       out_status;          /* [B] or NULL                             */
     float*         out_probs;           /* [B, vocab] kept-set probabilities, 0
                                            elsewhere (debug/oracle mode) or NULL   */
+    void*          workspace;           /* FG_SAMPLE_WORKSPACE_BYTES of device
+                                           memory, zero before the first call       */
 } FgSampleArgs;
+
+/*
+ * Workspace: rows are handed to the GPU's persistent CTAs through a counter in
+ * this small device buffer. The caller zeroes it once (cudaMemset) before its
+ * first use; every fg_sample call leaves it zeroed again. Calls that may run
+ * concurrently on the GPU (different streams) need separate workspaces.
+ */
+#define FG_SAMPLE_WORKSPACE_BYTES 256
 
 /*
  * Batched fused sampling (one decode step). Replaces Sampler.sample

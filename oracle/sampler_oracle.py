@@ -25,8 +25,11 @@ What it restates (paths inside the FlashGen project):
   whose cut falls inside a run of tied values (``tie_at_cut``).
 * ``sampler.py:120`` ``probs = softmax(filtered)``.
 * draw: the reference calls ``torch.multinomial``, which cannot be driven by a
-  caller-supplied uniform. Restated as an inverse CDF: the smallest id ``j``
-  (ascending id order) with ``sum_{i<=j} probs_i > u * sum(probs)``, in float64.
+  caller-supplied uniform. Restated as an inverse CDF over the kept tokens in
+  descending-probability order (ties in ascending id order), the order
+  FlashGen's native sampler draws in (``csrc/runtime/pipeline.cpp:311-340``):
+  the first token whose inclusive cumulative probability exceeds
+  ``u * sum(probs)``, accumulated in float64.
 
 Parity flags returned per row (a CUDA result may differ from the oracle only
 on flagged rows):
@@ -34,8 +37,13 @@ on flagged rows):
 * ``near_u``: ``u * S`` lies within ``1e-6 * S`` of a CDF boundary of the
   chosen token;
 * ``near_p``: the exclusive prefix mass of the last kept or first removed
-  token (in sorted order) lies within ``1e-6`` of ``top_p``;
-* ``tie_at_cut``: the top-p cut splits a run of equal values.
+  token (in sorted order) lies within ``1e-6`` of ``top_p``, or the
+  reference's own fp32 arithmetic (fp32 softmax over the sorted logits, whose
+  sum drops the many tiny tail terms) puts the cut on a different token than
+  the same computation in float64 — the cut then lies within the reference's
+  rounding error of ``top_p``;
+* ``tie_at_cut`` (informational): the top-p cut splits a run of equal values,
+  where the reference's unstable sort leaves the kept subset unspecified.
 """
 from __future__ import annotations
 
@@ -79,7 +87,8 @@ class OracleResult:
 
     @property
     def flagged(self) -> np.ndarray:
-        return self.near_u | self.near_p | self.tie_at_cut
+        """Rows on which a correct implementation may draw a different id."""
+        return self.near_u | self.near_p
 
 
 def apply_repetition_penalty_row(x: torch.Tensor, history: Sequence[int],
@@ -137,27 +146,43 @@ def top_p_filter(logit: torch.Tensor, p: float, stable: bool = True):
         if n_keep >= 1 and float(sorted_logits[n_keep - 1]) == float(sorted_logits[n_keep]) \
                 and float(sorted_logits[n_keep]) != float("-inf"):
             tie = True
+    # the same cut in float64 (exact to ~1e-16): a different position means the
+    # reference's fp32 rounding decided the cut
+    s64 = sorted_logits.to(torch.float64)
+    e64 = torch.exp(s64 - s64[0])
+    p64 = e64 / e64.sum()
+    excl64 = torch.cumsum(p64, 0) - p64
+    n_keep64 = int((~(excl64 > p)).sum())
+    if n_keep64 != n_keep:
+        near = True
+    elif n_keep64 < V:
+        for j in (n_keep64 - 1, n_keep64):
+            if 0 <= j < V and abs(float(excl64[j]) - p) < NEAR_TOL:
+                near = True
     sorted_logits = sorted_logits.masked_fill(remove, float("-inf"))
     return logit.scatter(0, sorted_indices, sorted_logits), near, tie
 
 
-def inverse_cdf(probs: torch.Tensor, u: float):
-    """Smallest ascending id j with cumsum_f64(probs)[j] > u * sum(probs).
+def inverse_cdf(filtered: torch.Tensor, probs: torch.Tensor, u: float):
+    """Inverse CDF over the kept tokens (filtered != -inf) in descending value
+    order, ties in ascending id order; cumulative sums in float64.
 
-    Returns (j, near_u).
+    Returns (token id, near_u).
     """
-    p64 = probs.to(torch.float64).numpy()
+    kept = torch.nonzero(filtered != float("-inf")).flatten()
+    order = kept[torch.sort(filtered[kept], descending=True, stable=True).indices]
+    p64 = probs[order].to(torch.float64).numpy()
     cdf = np.cumsum(p64)
     total = float(cdf[-1])
     target = float(np.float64(np.float32(u))) * total
     j = int(np.searchsorted(cdf, target, side="right"))
     j = min(j, len(p64) - 1)
-    while j > 0 and p64[j] == 0.0:   # never land on a zero-probability id
+    while j > 0 and p64[j] == 0.0:   # never land on a zero-probability token
         j -= 1
     lo = cdf[j - 1] if j > 0 else 0.0
     hi = cdf[j]
     near = abs(target - lo) < NEAR_TOL * total or abs(hi - target) < NEAR_TOL * total
-    return j, near
+    return int(order[j]), near
 
 
 def sample_rows(logits: torch.Tensor, params: RowParams,
@@ -205,7 +230,7 @@ def sample_rows(logits: torch.Tensor, params: RowParams,
                 kept_ids.append(np.zeros(0, dtype=np.int64))
                 kept_probs.append(np.zeros(0, dtype=np.float32))
             continue
-        j, near_u[r] = inverse_cdf(probs, float(uniforms[r]))
+        j, near_u[r] = inverse_cdf(x, probs, float(uniforms[r]))
         ids[r] = j
         if want_kept:
             nz = torch.nonzero(x != float("-inf")).flatten()

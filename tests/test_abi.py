@@ -64,6 +64,9 @@ def test_validation_without_gpu():
     assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # bad dtype
     a.dtype = _lib.FG_DTYPE_F32
     a.temperature = a.top_p = a.top_k = a.uniforms = a.out_ids = 16
+    a.row_stride, a.batch = 8, 0
+    assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # no workspace
+    a.workspace, a.batch = 256, 1
     a.row_stride = 4
     assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # stride < vocab
     a.row_stride, a.batch = 8, 0

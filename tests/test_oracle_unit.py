@@ -26,12 +26,14 @@ def test_top_p_tie_order_is_ascending_id():
     assert tie
 
 
-def test_inverse_cdf_ascending_ids():
-    p = torch.tensor([0.0, 0.25, 0.0, 0.5, 0.25])
-    assert O.inverse_cdf(p, 0.0)[0] == 1
-    assert O.inverse_cdf(p, 0.2499)[0] == 1
-    assert O.inverse_cdf(p, 0.26)[0] == 3
-    assert O.inverse_cdf(p, 0.9999)[0] == 4
+def test_inverse_cdf_descending_probability():
+    x = torch.log(torch.tensor([0.0, 0.25, 0.0, 0.5, 0.25]))   # order: 3, then ties 1, 4
+    p = torch.softmax(x, -1)
+    assert O.inverse_cdf(x, p, 0.0)[0] == 3
+    assert O.inverse_cdf(x, p, 0.4999)[0] == 3
+    assert O.inverse_cdf(x, p, 0.51)[0] == 1
+    assert O.inverse_cdf(x, p, 0.76)[0] == 4
+    assert O.inverse_cdf(x, p, 0.9999)[0] == 4
 
 
 def test_penalties_order():
