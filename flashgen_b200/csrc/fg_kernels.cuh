@@ -188,13 +188,16 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
         run += __popc(s.bitmap[2 * q]) + (2 * q + 1 < nw ? __popc(s.bitmap[2 * q + 1]) : 0);
     }
     csync();
-    // ascending list of distinct columns: warp-parallel over words (a lane per bit)
-    for (int w0 = (tid >> 5); w0 < nw; w0 += NCW) {
-        const uint32_t bits = s.bitmap[w0];
+    // ascending list of distinct columns: words strided over the threads
+    for (int w = tid; w < nw; w += NCT) {
+        uint32_t bits = s.bitmap[w];
         if (bits == 0u) continue;
-        if ((bits >> lane) & 1u) {
-            const uint32_t rk = hist_rank(s, (uint32_t)(w0 * 32 + lane));
-            if (rk < cap) s.scol[rk] = (uint32_t)(w0 * 32 + lane);
+        uint32_t rk = hist_rank(s, (uint32_t)(w * 32));
+        while (bits) {
+            const int b = __ffs(bits) - 1;
+            bits &= bits - 1;
+            if (rk < cap) s.scol[rk] = (uint32_t)(w * 32 + b);
+            ++rk;
         }
     }
     const uint32_t U = min(total, cap);
@@ -221,7 +224,7 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
                 bool v = i < h1 && gid >= 0 && gid < P.vocab_total && c >= 0 && c < P.vocab;
                 const uint32_t rk = v ? hist_rank(s, (uint32_t)c) : 0u;
                 v = v && rk < U;
-                agg_add<true>(s.counts, nullptr, v, rk, 0ull, lane);
+                if (v) atomicAdd(&s.counts[rk], 1u);
             }
         }
     }
@@ -259,36 +262,17 @@ struct Stream {
     bool cand;
     uint32_t base;        // candidates before the current window
     uint32_t win;         // window index (counter slot = win % 3)
+    uint32_t khi, klo;    // key range of this thread's appends
 };
 
-// Warp-aggregated append of the items selected by `pick` (bit i selects item i;
-// item(i, key, col) returns them).
-template <class Item>
-__device__ __forceinline__ void warp_append(const Smem& s, Stream& st, uint32_t pick, int lane, Item&& item) {
-    const uint32_t cnt = __popc(pick);
-    const uint32_t incl = warp_incl_scan_u32(cnt, lane);
-    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-    if (total == 0) return;
+// Append one candidate (no warp collectives: 32-bit shared atomics on one
+// counter are combined by the hardware). The key range is tracked per thread
+// and reduced only when a compaction needs it.
+__device__ __forceinline__ void append1(const Smem& s, Stream& st, uint32_t key, uint32_t col) {
     const int slot = (int)(st.win % 3u);
-    uint32_t base = 0;
-    if (lane == 31) base = atomicAdd(&s.ctl->wcnt[slot], total);
-    base = __shfl_sync(0xffffffffu, base, 31) + st.base;
-    uint32_t pos = base + incl - cnt;
-    uint32_t kmax = 0, kmin = 0xffffffffu;
-    bool ovf = false;
-    while (pick) {
-        const int i = __ffs(pick) - 1;
-        pick &= pick - 1;
-        uint32_t key, col;
-        item(i, key, col);
-        if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = key; s.cid[pos] = col; } else ovf = true;
-        ++pos;
-        kmax = max(kmax, key); kmin = min(kmin, key);
-    }
-    kmax = __reduce_max_sync(0xffffffffu, kmax);
-    kmin = __reduce_min_sync(0xffffffffu, kmin);
-    if (__any_sync(0xffffffffu, ovf) && lane == 0) s.ctl->ovf[slot] = 1;
-    if (lane == 0) { atomicMax(&s.ctl->hikey, kmax); atomicMin(&s.ctl->lokey, kmin); }
+    const uint32_t pos = st.base + atomicAdd(&s.ctl->wcnt[slot], 1u);
+    if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = key; s.cid[pos] = col; } else s.ctl->ovf[slot] = 1;
+    st.khi = max(st.khi, key); st.klo = min(st.klo, key);
 }
 
 // One element outside the streamed interior (ragged columns, merged history).
@@ -308,23 +292,18 @@ __device__ __forceinline__ void process_one(const RowParams& p, const Smem& s, S
             st.z0 += ex2_approx(__fmaf_rn(x, p.c, st.nzmc));
         }
     }
-    if (st.cand) {
-        const uint32_t pick = (valid && x >= st.xmin) ? 1u : 0u;
-        if (__any_sync(0xffffffffu, pick)) {
-            const uint32_t key = fkey(x);
-            warp_append(s, st, pick, lane, [&](int, uint32_t& k, uint32_t& c) { k = key; c = col; });
-        }
-    }
+    if (st.cand && valid && x >= st.xmin) append1(s, st, fkey(x), col);
 }
 
 // ---------------------------------------------------------------------------
 // Compaction: exact K-th largest candidate key -> xmin; drop keys below it
 // (stable, in place). Returns the new candidate count.
 // ---------------------------------------------------------------------------
-__device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t n) {
+__device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t n, Stream& st) {
     RowCtl* ctl = s.ctl;
-    const uint32_t lo = ctl->lokey, hi = ctl->hikey;
-    if (n <= (uint32_t)p.K || lo > hi) return n;
+    if (n <= (uint32_t)p.K) return n;
+    const uint32_t lo = cons_min_u32(st.klo, s, tid), hi = cons_max_u32(st.khi, s, tid);
+    if (lo > hi) return n;
     const SelOut so = block_select<true, true>(
         [&](auto&& f) {
             for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
@@ -337,10 +316,10 @@ __device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t
     if (tid == 0) {
         const float xm = xmin_for(p, funkey(so.key));
         if (xm > ctl->xmin) ctl->xmin = xm;
-        ctl->lokey = fkey(ctl->xmin);
     }
     csync();
     const uint32_t kmin = fkey(ctl->xmin);
+    st.klo = max(st.klo, kmin);
     uint32_t out = 0;
     for (uint32_t base = 0; base < n; base += NCT * 8) {
         uint32_t kk[8], ii[8], keep = 0, cnt = 0;
@@ -376,7 +355,7 @@ __device__ __forceinline__ void window_check(const RowParams& p, const Smem& s, 
         if (ovf) {
             st.cand = false;
         } else if (n > limit) {
-            n = compact(p, s, tid, n);
+            n = compact(p, s, tid, n, st);
             if (n > limit) st.cand = false;
         }
         st.xmin = s.ctl->xmin;
@@ -478,21 +457,22 @@ __device__ Located locate(const KParams& P, const Smem& s, const RowParams& p, i
         return t >= (float)(NB - 1) ? (uint32_t)(NB - 1) : (uint32_t)t;
     };
     uint32_t* cn = s.cnts;
-    unsigned long long* bn = s.bins;
+    uint32_t* bl = s.blo;
+    uint32_t* bh = s.bhi;
     // ---- level 0: linear bins ----
-    cn[tid] = 0u; bn[tid] = 0ull;
+    cn[tid] = 0u; bl[tid] = 0u; bh[tid] = 0u;
     csync();
     for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
         const float y = ydiv(p, x);
         const uint32_t k = fkey(y);
         const bool v = valid && k >= rlo && k <= rhi;
-        agg_add<false>(cn, bn, v, lbin(y), v ? q_of(efast(y, My), scale) : 0ull, lane);
+        add_bin<false>(cn, bl, bh, v, lbin(y), v ? q_of(efast(y, My), scale) : 0ull);
     });
     csync();
-    L.total = cons_sum_u64(bn[tid], s, tid);
+    L.total = cons_sum_u64(bin_mass(bl, bh, tid), s, tid);
     if (L.total == 0) return L;
     if (target >= L.total) target = L.total - 1;
-    if (tid < 32) warp0_scan_bins<true, false>(s, cn, bn, NB, target, 0, tid);
+    if (tid < 32) warp0_scan_bins<true, false>(s, cn, bl, bh, NB, target, 0, tid);
     csync();
     const SelSlot r0 = s.ctl->sel[0];
     csync();
@@ -526,16 +506,16 @@ __device__ Located locate(const KParams& P, const Smem& s, const RowParams& p, i
             const int shift = rem - w;
             const uint32_t dmask = (1u << w) - 1u;
             const int nb = 1 << w;
-            cn[tid] = 0u; bn[tid] = 0ull;
+            cn[tid] = 0u; bl[tid] = 0u; bh[tid] = 0u;
             csync();
             for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
                 const float y = ydiv(p, x);
                 const uint32_t k = fkey(y);
                 const bool v = valid && k >= rlo && k <= rhi && lbin(y) == b0 && (k & pmask) == prefix;
-                agg_add<false>(cn, bn, v, (k >> shift) & dmask, v ? q_of(efast(y, My), scale) : 0ull, lane);
+                add_bin<false>(cn, bl, bh, v, (k >> shift) & dmask, v ? q_of(efast(y, My), scale) : 0ull);
             });
             csync();
-            if (tid < 32) warp0_scan_bins<true, false>(s, cn, bn, nb, target - before, pass & 1, tid);
+            if (tid < 32) warp0_scan_bins<true, false>(s, cn, bl, bh, nb, target - before, pass & 1, tid);
             csync();
             const SelSlot rr = s.ctl->sel[pass & 1];
             csync();
@@ -694,24 +674,8 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
     st.zm = -1e30f; st.nzmc = -(st.zm * p.c); st.z0 = 0.0f; st.z1 = 0.0f;
     st.xmin = -INFINITY; st.cand = p.cand; st.base = 0; st.win = 0;
     st.bestv = -INFINITY; st.bestc = 0xffffffffu;
+    st.khi = 0u; st.klo = 0xffffffffu;
     const uint8_t* rowp = reinterpret_cast<const uint8_t*>(P.logits) + (int64_t)r * P.row_stride * ESZ;
-
-    // ---- ragged head/tail columns (at most 2 * (VEC - 1)), one per lane of warp 0 ----
-    if (warp == 0) {
-        const int nh = g.head, nt = P.vocab - g.tail0;
-        bool valid = lane < nh + nt;
-        const int c = lane < nh ? lane : g.tail0 + (lane - nh);
-        float x = -INFINITY;
-        if (valid) {
-            x = E::load(rowp, c);
-            if (p.pen && (hist_bits(s, P.nwords, c, 1) & 1u)) {
-                const uint32_t rk = hist_rank(s, (uint32_t)c);
-                if (rk < U) s.sval[rk] = x;   // merged after the stream
-                valid = false;
-            }
-        }
-        process_one(p, s, st, x, (uint32_t)(valid ? c : 0), valid, lane);
-    }
 
     // ---- streamed interior ----
     for (int t = 0; t < g.ntiles; ++t) {
@@ -775,6 +739,13 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
 #pragma unroll
                 for (int j = 0; j < CPT; ++j) cm[j] = chunk_max1<DT>(v[j]);
                 const int K = p.K;
+                // key range of the values the select will see
+                float lo_v = INFINITY;
+                if (K <= NCT / 2) lo_v = m;
+                else if (K <= NCT) { for (int j = 0; j < CPT; ++j) lo_v = fminf(lo_v, cm[j]); }
+                else lo_v = chunks_min<DT>(v);
+                const uint32_t klo = cons_min_u32((lo_v == lo_v && lo_v > -INFINITY) ? fkey(lo_v) : 0xffffffffu, s, tid);
+                const uint32_t khi = cons_max_u32((m == m && m > -INFINITY) ? fkey(m) : 0u, s, tid);
                 const SelOut so = block_select<true, true>(
                     [&](auto&& f) {
                         if (K <= NCT / 2) {
@@ -792,7 +763,7 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
                                 }
                         }
                     },
-                    (uint64_t)(K - 1), 0u, 32, s, tid);
+                    (uint64_t)(K - 1), klo <= khi ? klo : 0u, klo <= khi ? varying_bits(klo, khi) : 32, s, tid);
                 if (so.ok && tid == 0) {
                     const float xm = xmin_for(p, funkey(so.key));
                     if (xm > ctl->xmin) ctl->xmin = xm;
@@ -812,15 +783,14 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
                     }
                 }
             }
-            if (__any_sync(0xffffffffu, pick)) {
-                warp_append(s, st, pick, lane, [&](int i, uint32_t& key, uint32_t& col) {
-                    const int j = i / VEC, e = i % VEC;
-                    uint4 vv = v[0];
+            while (pick) {
+                const int i = __ffs(pick) - 1;
+                pick &= pick - 1;
+                const int j = i / VEC, e = i % VEC;
+                uint4 vv = v[0];
 #pragma unroll
-                    for (int jj = 1; jj < CPT; ++jj) if (jj == j) vv = v[jj];
-                    key = fkey(elem_get<DT>(vv, e));
-                    col = (uint32_t)(tcol0 + (tid + j * NCT) * VEC + e);
-                });
+                for (int jj = 1; jj < CPT; ++jj) if (jj == j) vv = v[jj];
+                append1(s, st, fkey(elem_get<DT>(vv, e)), (uint32_t)(tcol0 + (tid + j * NCT) * VEC + e));
             }
             // appends per tile fall off as 1/t: check every tile early in the
             // row, every 2nd and then every 4th tile later (appends are bounds
@@ -828,6 +798,24 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
             const bool chk = t < 8 || (t < 16 ? (t & 1) == 1 : (t & 3) == 3) || t == g.ntiles - 1;
             if (chk) window_check(p, s, tid, st, (uint32_t)HWM);
         }
+    }
+
+    // ---- ragged head/tail columns (at most 2 * (VEC - 1)), one per lane of warp 0;
+    //      processed after the interior so the candidate filter is final ----
+    if (warp == 0) {
+        const int nh = g.head, nt = P.vocab - g.tail0;
+        bool valid = lane < nh + nt;
+        const int c = lane < nh ? lane : g.tail0 + (lane - nh);
+        float x = -INFINITY;
+        if (valid) {
+            x = E::load(rowp, c);
+            if (p.pen && (hist_bits(s, P.nwords, c, 1) & 1u)) {
+                const uint32_t rk = hist_rank(s, (uint32_t)c);
+                if (rk < U) s.sval[rk] = x;   // merged after the stream
+                valid = false;
+            }
+        }
+        process_one(p, s, st, x, (uint32_t)(valid ? c : 0), valid, lane);
     }
 
     // ---- merge the history columns with their penalised values ----

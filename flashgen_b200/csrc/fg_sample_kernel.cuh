@@ -107,7 +107,8 @@ struct Smem {
     float* redf;
     uint32_t* red32;
     double* redd;
-    unsigned long long* bins;  // [2][NB]
+    uint32_t* blo;             // [2][NB] low words of the bin masses
+    uint32_t* bhi;             // [2][NB] high words
     uint32_t* cnts;            // [2][NB]
     uint32_t* ckey;            // [CAND_CAP]
     uint32_t* cid;             // [CAND_CAP]
@@ -142,7 +143,8 @@ __device__ __forceinline__ Smem carve(uint8_t* base, const KParams& P) {
     s.redd = reinterpret_cast<double*>(base + o); o += 8 * NCW;
     s.redf = reinterpret_cast<float*>(base + o); o += 4 * NCW;
     s.red32 = reinterpret_cast<uint32_t*>(base + o);
-    s.bins = reinterpret_cast<unsigned long long*>(base + P.off_bins);
+    s.blo = reinterpret_cast<uint32_t*>(base + P.off_bins);
+    s.bhi = s.blo + 2 * NB;
     s.cnts = reinterpret_cast<uint32_t*>(base + P.off_cnts);
     s.ckey = reinterpret_cast<uint32_t*>(base + P.off_ckey);
     s.cid = reinterpret_cast<uint32_t*>(base + P.off_cid);
@@ -351,38 +353,27 @@ __device__ __forceinline__ uint32_t cons_excl_scan_u32(uint32_t v, uint32_t& tot
 }
 
 // ---------------------------------------------------------------------------
-// Warp-aggregated histogram add. Every lane of the warp calls it (valid says
-// whether the lane contributes). Lanes with the same digit are grouped with
-// match.any: the group leader adds the group's count, and the group's 64-bit
-// weight sum (three exact 21-bit partial sums), so no bin sees more than one
-// atomic per warp instruction.
+// Histogram add: count, and (unless COUNT) a 64-bit weight as two 32-bit
+// atomics with an exact carry (the returned old low word tells whether this
+// addition wrapped). 64-bit shared-memory atomics are avoided: under contention
+// they cost ~70x a 32-bit one on sm_100a.
 // ---------------------------------------------------------------------------
 template <bool COUNT>
-__device__ __forceinline__ void agg_add(uint32_t* cnts, unsigned long long* bins, bool valid, uint32_t d, uint64_t w,
-                                        int lane) {
-    const uint32_t vm = __ballot_sync(0xffffffffu, valid);
-    if (vm == 0u) return;
-    const uint32_t key = valid ? d : (0x80000000u | (uint32_t)lane);
-    const uint32_t peers = __match_any_sync(0xffffffffu, key) & vm;
-    const bool leader = valid && lane == __ffs(peers) - 1;
-    if (leader) atomicAdd(&cnts[d], (uint32_t)__popc(peers));
-    if (COUNT) return;
-    const bool solo = __popc(peers) == 1;
-    if (valid && solo && w) atomicAdd(&bins[d], (unsigned long long)w);
-    uint32_t todo = __ballot_sync(0xffffffffu, leader && !solo);
-    while (todo) {
-        const int ldr = __ffs(todo) - 1;
-        todo &= todo - 1;
-        const uint32_t grp = __shfl_sync(0xffffffffu, peers, ldr);
-        const uint64_t part = ((grp >> lane) & 1u) ? w : 0ull;
-        const uint32_t s0 = __reduce_add_sync(0xffffffffu, (uint32_t)(part & 0x1fffffu));
-        const uint32_t s1 = __reduce_add_sync(0xffffffffu, (uint32_t)((part >> 21) & 0x1fffffu));
-        const uint32_t s2 = __reduce_add_sync(0xffffffffu, (uint32_t)(part >> 42));
-        if (lane == ldr) {
-            const uint64_t tot = (uint64_t)s0 + ((uint64_t)s1 << 21) + ((uint64_t)s2 << 42);
-            if (tot) atomicAdd(&bins[d], (unsigned long long)tot);
-        }
+__device__ __forceinline__ void add_bin(uint32_t* cnts, uint32_t* blo, uint32_t* bhi, bool valid, uint32_t d,
+                                        uint64_t w) {
+    if (!valid) return;
+    atomicAdd(&cnts[d], 1u);
+    if (COUNT || w == 0) return;
+    const uint32_t l = (uint32_t)w;
+    uint32_t h = (uint32_t)(w >> 32);
+    if (l) {
+        const uint32_t old = atomicAdd(&blo[d], l);
+        h += (old + l < old) ? 1u : 0u;
     }
+    if (h) atomicAdd(&bhi[d], h);
+}
+__device__ __forceinline__ uint64_t bin_mass(const uint32_t* blo, const uint32_t* bhi, int d) {
+    return ((uint64_t)bhi[d] << 32) | blo[d];
 }
 
 // ---------------------------------------------------------------------------
@@ -427,15 +418,15 @@ __device__ __forceinline__ uint64_t block_incl_scan_u64(uint64_t v, const Smem& 
 // ascending) digit order and writes, to sel[slot], the digit whose bin holds
 // `rel` (ok = 0 when rel >= total). Lane l owns scan positions [8l, 8l + 8).
 template <bool DESC, bool COUNT>
-__device__ __forceinline__ void warp0_scan_bins(const Smem& s, const uint32_t* cn, const unsigned long long* bn,
-                                                int nb, uint64_t rel, int slot, int lane) {
+__device__ __forceinline__ void warp0_scan_bins(const Smem& s, const uint32_t* cn, const uint32_t* bl,
+                                                const uint32_t* bh, int nb, uint64_t rel, int slot, int lane) {
     uint64_t v[8];
     uint64_t lsum = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int o = lane * 8 + j;
         const int d = DESC ? nb - 1 - o : o;
-        v[j] = (o < nb) ? (COUNT ? (uint64_t)cn[d] : (uint64_t)bn[d]) : 0ull;
+        v[j] = (o < nb) ? (COUNT ? (uint64_t)cn[d] : bin_mass(bl, bh, d)) : 0ull;
         lsum += v[j];
     }
     const uint64_t incl = warp_incl_scan_u64(lsum, lane);
@@ -455,7 +446,7 @@ __device__ __forceinline__ void warp0_scan_bins(const Smem& s, const uint32_t* c
         if (jj > 7) jj = 7;
         const int d = DESC ? nb - 1 - (lane * 8 + jj) : lane * 8 + jj;
         o.ok = 1; o.digit = (uint32_t)d; o.before = c; o.nat = cn[d];
-        o.at = COUNT ? (uint64_t)cn[d] : (uint64_t)bn[d];
+        o.at = COUNT ? (uint64_t)cn[d] : bin_mass(bl, bh, d);
     }
 }
 
@@ -463,6 +454,7 @@ template <bool DESC, bool COUNT, class Enum>
 __device__ SelOut block_select(Enum&& enumerate, uint64_t target, uint32_t prefix, int rem, const Smem& s,
                                int tid) {
     const int lane = tid & 31;
+    (void)lane;
     SelOut out;
     uint32_t pmask = rem >= 32 ? 0u : ~((1u << rem) - 1u);
     prefix &= pmask;
@@ -481,24 +473,25 @@ __device__ SelOut block_select(Enum&& enumerate, uint64_t target, uint32_t prefi
     bool ok = true;
     int buf = 0, pass = 0;
     s.cnts[tid] = 0u;
-    if (!COUNT) s.bins[tid] = 0ull;
+    if (!COUNT) { s.blo[tid] = 0u; s.bhi[tid] = 0u; }
     csync();
     while (rem > 0) {
         const int w = rem < 8 ? rem : 8;
         const int shift = rem - w;
         const uint32_t dmask = (1u << w) - 1u;
         uint32_t* cn = s.cnts + buf * NB;
-        unsigned long long* bn = s.bins + buf * NB;
+        uint32_t* bl = s.blo + buf * NB;
+        uint32_t* bh = s.bhi + buf * NB;
         // clear the other buffer for the next pass (it was last read before the
         // previous pass's second barrier)
         s.cnts[(buf ^ 1) * NB + tid] = 0u;
-        if (!COUNT) s.bins[(buf ^ 1) * NB + tid] = 0ull;
+        if (!COUNT) { s.blo[(buf ^ 1) * NB + tid] = 0u; s.bhi[(buf ^ 1) * NB + tid] = 0u; }
         enumerate([&](bool valid, uint32_t k, uint64_t wt) {
             const bool v = valid && ((k & pmask) == prefix);
-            agg_add<COUNT>(cn, bn, v, (k >> shift) & dmask, wt, lane);
+            add_bin<COUNT>(cn, bl, bh, v, (k >> shift) & dmask, wt);
         });
         csync();
-        if (tid < 32) warp0_scan_bins<DESC, COUNT>(s, cn, bn, 1 << w, target - before, pass & 1, lane);
+        if (tid < 32) warp0_scan_bins<DESC, COUNT>(s, cn, bl, bh, 1 << w, target - before, pass & 1, lane);
         csync();
         const SelSlot r = s.ctl->sel[pass & 1];
         if (!r.ok) { ok = false; break; }

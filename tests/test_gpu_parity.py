@@ -200,3 +200,17 @@ def test_argmax_and_rep_penalty(cuda_device):
         out = Sampler().apply_repetition_penalty(x.cuda(), hist, 1.3).cpu()
         iv = torch.int32 if dt == torch.float32 else torch.int16
         assert torch.equal(out.view(iv), ref.view(iv)), dt
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_unaligned_rows_large_nucleus(cuda_device, seed):
+    # rows that start off a 16-byte boundary have ragged columns outside the
+    # streamed interior; with a nucleus larger than the candidate target the
+    # cut is found by the multi-pass path, which must count every column once
+    g = torch.Generator().manual_seed(seed)
+    B, V = 6, 20001
+    logits = torch.randn(B, V, generator=g).to(torch.float16)
+    p = BatchParams.uniform(B, temperature=1.1, top_p=0.9, top_k=-1)
+    p.top_p[:] = [0.9, 0.97, 0.5, 0.999, 0.8, 0.95]
+    stats, ids, status = _check(_workload(logits, p, seed=seed))
+    assert (status & _lib.FG_ROW_GENERAL_PATH).any()
