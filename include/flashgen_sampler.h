@@ -82,8 +82,10 @@ extern "C" {
  * temperature (x / T when T != 1), top-k (keep every logit >= the k-th
  * largest; k <= 0 disables), top-p (keep the descending prefix whose exclusive
  * mass is <= top_p, ties at the cut in ascending id order; top_p >= 1
- * disables), softmax, and an inverse-CDF draw: the smallest id j, in ascending
- * id order over the kept set, whose inclusive mass exceeds u * total.
+ * disables), softmax, and an inverse-CDF draw over the kept set walked in
+ * descending-probability order (ties in ascending id order), the order of
+ * csrc/runtime/pipeline.cpp:311-340: the first token whose inclusive mass
+ * exceeds u * total.
  *
  * Histories: CSR token lists. Row r's ids are hist_ids[hist_offsets[r] ..
  * hist_offsets[r+1]). Ids are global vocabulary ids in [0, vocab_total);
