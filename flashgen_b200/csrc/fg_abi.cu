@@ -161,6 +161,7 @@ int fg_sample(const FgSampleArgs* a, void* stream) {
     }
     if (chosen == 0) return FG_ENOTSUP;
     P.nstage = chosen;
+    P.off_ctl = fg::ctl_offset(chosen);
     const int grid = std::min(a->batch, d->sms * per_sm);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     switch (a->dtype) {

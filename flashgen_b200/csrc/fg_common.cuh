@@ -5,6 +5,7 @@
 // and block-level reductions over a named barrier.
 #pragma once
 
+#include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -160,6 +161,55 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         }
     }
 }
+// ---- 32-bit shared-window addresses (the streaming loop keeps no 64-bit
+//      pointers live: its addresses are a symbol plus grid-constant offsets)
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void sts_u32(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" :: "r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atoms_add_u32(uint32_t a, uint32_t v) {
+    uint32_t o;
+    asm volatile("atom.shared.add.u32 %0, [%1], %2;" : "=r"(o) : "r"(a), "r"(v) : "memory");
+    return o;
+}
+__device__ __forceinline__ bool mbar_test_a(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive_a(uint32_t bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" :: "r"(bar) : "memory");
+}
+// mbar_wait on a shared-window address; the abort flag is the int at `abort_a`.
+__device__ __forceinline__ bool mbar_wait_a(uint32_t bar, uint32_t parity, uint32_t abort_a) {
+    if (mbar_test_a(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_test_a(bar, parity)) return true;
+        if ((it & 63u) == 63u) {
+            if (lds_u32(abort_a) != 0u) return false;
+            if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) return false;
+        }
+    }
+}
+
 // Wait for phase `parity` of `bar` for at most `limit_ns`; returns false on expiry.
 __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     const uint64_t t0 = globaltimer_ns();
@@ -172,6 +222,24 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, ui
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// Same copy with an L2 cache policy (createpolicy) attached to the reads.
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy) : "memory");
+}
+// L2 policy that keeps the lines it fills ahead of normal lines.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// Return the 128-byte L2 line holding `p` to the normal eviction priority.
+__device__ __forceinline__ void l2_evict_normal(const void* p) {
+    asm volatile("applypriority.global.L2::evict_normal [%0], 128;" :: "l"(p) : "memory");
 }
 
 // Named barrier over the first `nthreads` threads of the block (id != 0).

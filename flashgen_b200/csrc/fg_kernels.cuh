@@ -24,9 +24,6 @@ template <> struct Neg<FG_DTYPE_F32> { static constexpr uint32_t W = 0xFF800000u
 template <> struct Neg<FG_DTYPE_F16> { static constexpr uint32_t W = 0xFC00FC00u; };
 template <> struct Neg<FG_DTYPE_BF16> { static constexpr uint32_t W = 0xFF80FF80u; };
 
-__device__ __forceinline__ uint32_t& word_of(uint4& v, int q) {
-    return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
-}
 __device__ __forceinline__ uint32_t word_get(const uint4& v, int q) {
     return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
 }
@@ -41,13 +38,25 @@ __device__ __forceinline__ float elem_get(const uint4& v, int e) {
         else return __half2float(__ushort_as_half(h));
     }
 }
+// Element e of a chunk set to -inf. Written as selects on the four words: a
+// reference to a word chosen at run time would force the chunk (and with it
+// the tile's registers) into local memory.
 template <int DT>
 __device__ __forceinline__ void elem_mask(uint4& v, int e) {
     if constexpr (DT == FG_DTYPE_F32) {
-        word_of(v, e) = Neg<DT>::W;
+        constexpr uint32_t W = Neg<DT>::W;
+        v.x = e == 0 ? W : v.x;
+        v.y = e == 1 ? W : v.y;
+        v.z = e == 2 ? W : v.z;
+        v.w = e == 3 ? W : v.w;
     } else {
-        uint32_t& w = word_of(v, e >> 1);
-        w = (e & 1) ? ((w & 0x0000ffffu) | (Neg<DT>::W & 0xffff0000u)) : ((w & 0xffff0000u) | (Neg<DT>::W & 0xffffu));
+        const int q = e >> 1;
+        const uint32_t keep = (e & 1) ? 0x0000ffffu : 0xffff0000u;
+        const uint32_t neg = Neg<DT>::W & ~keep;
+        v.x = q == 0 ? ((v.x & keep) | neg) : v.x;
+        v.y = q == 1 ? ((v.y & keep) | neg) : v.y;
+        v.z = q == 2 ? ((v.z & keep) | neg) : v.z;
+        v.w = q == 3 ? ((v.w & keep) | neg) : v.w;
     }
 }
 
@@ -342,25 +351,81 @@ __device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t
     return out;
 }
 
-// End of a candidate window: uniform candidate count, compaction when the
-// buffer passed `limit`.
-__device__ __forceinline__ void window_check(const RowParams& p, const Smem& s, int tid, Stream& st, uint32_t limit) {
+// End of a candidate window, without any call (the streaming loop must not
+// contain one): uniform candidate count, overflow, and whether the buffer must
+// be compacted before the next window (it passed `limit`, or the next tile
+// could overflow it at twice this window's append rate). Sets st.base to the
+// count and rate2 to twice this window's appends.
+__device__ __forceinline__ bool window_end(uint32_t a_ctl, int tid, Stream& st, uint32_t limit, uint64_t& rate2) {
+    csync();
+    const uint32_t slot = st.win % 3u;
+    const uint32_t n = st.base + lds_u32(a_ctl + (uint32_t)offsetof(RowCtl, wcnt) + 4u * slot);
+    const bool ovf = lds_u32(a_ctl + (uint32_t)offsetof(RowCtl, ovf) + 4u * slot) != 0u;
+    if (tid == 0) {
+        const uint32_t nx = (slot + 2u) % 3u;
+        sts_u32(a_ctl + (uint32_t)offsetof(RowCtl, wcnt) + 4u * nx, 0u);
+        sts_u32(a_ctl + (uint32_t)offsetof(RowCtl, ovf) + 4u * nx, 0u);
+    }
+    st.win += 1;
+    rate2 = 2ull * (uint64_t)(n - st.base);
+    st.base = n;
+    if (!st.cand) return false;
+    if (ovf) { st.cand = false; return false; }
+    return n > limit || (uint64_t)n + rate2 + 64ull > (uint64_t)CAND_CAP;
+}
+// Tiles (a power of two <= span_max) the next window may cover with n
+// candidates at rate2 / span appends per tile.
+__device__ __forceinline__ int window_span(uint32_t n, uint64_t rate2, int span, int span_max) {
+    int next = span_max;
+    const uint64_t sp = (uint64_t)(span > 0 ? span : 1);
+    while (next > 1 && (uint64_t)n + rate2 * (uint64_t)next / sp + 64ull > (uint64_t)CAND_CAP) next >>= 1;
+    return next;
+}
+__device__ __forceinline__ int span_max_at(int t) { return t < 4 ? 1 : (t < 16 ? 4 : 8); }
+
+// End of a candidate window of `span` tiles: uniform candidate count, then a
+// compaction when the buffer passed `limit` or when the next window could
+// overflow it at twice this window's append rate. Returns the number of tiles
+// (a power of two <= span_max) the next window may cover at that rate.
+__device__ __forceinline__ uint32_t compact_cold(const KParams& P, int tid, int r, uint32_t n, uint32_t klo,
+                                              uint32_t khi) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    Stream st;
+    st.klo = klo;
+    st.khi = khi;
+    return compact(p, s, tid, n, st);
+}
+
+__device__ __forceinline__ int window_check(const KParams& P, int r, const RowParams& p, const Smem& s, int tid,
+                                           Stream& st, uint32_t limit, int span, int span_max) {
     csync();
     const int slot = (int)(st.win % 3u);
     uint32_t n = st.base + s.ctl->wcnt[slot];
     const bool ovf = s.ctl->ovf[slot] != 0;
     if (tid == 0) { s.ctl->wcnt[(slot + 2) % 3] = 0u; s.ctl->ovf[(slot + 2) % 3] = 0; }
     st.win += 1;
+    int next = span_max;
     if (st.cand) {
         if (ovf) {
             st.cand = false;
-        } else if (n > limit) {
-            n = compact(p, s, tid, n, st);
-            if (n > limit) st.cand = false;
+        } else {
+            const uint64_t rate2 = 2ull * (uint64_t)(n - st.base);   // twice the appends of this window
+            auto fits = [&](uint32_t nn, int sp) {
+                return (uint64_t)nn + rate2 * (uint64_t)sp / (uint64_t)(span > 0 ? span : 1) + 64ull <=
+                       (uint64_t)CAND_CAP;
+            };
+            if (n > limit || !fits(n, 1)) {
+                n = compact_cold(P, tid, r, n, st.klo, st.khi);
+                st.klo = max(st.klo, fkey(s.ctl->xmin));
+                if (n > limit) st.cand = false;
+            }
+            while (next > 1 && !fits(n, next)) next >>= 1;
         }
         st.xmin = s.ctl->xmin;
     }
     st.base = n;
+    return next;
 }
 
 // ---------------------------------------------------------------------------
@@ -384,14 +449,26 @@ __device__ __forceinline__ void for_row(const KParams& P, const Smem& s, const R
         }
         f(valid, valid ? c : 0, x);
     }
+    // RUN chunks per thread are loaded before any is processed, so a pass over
+    // a row re-read from L2 keeps RUN * NCT * 16 bytes in flight per CTA.
+    constexpr int RUN = 4;
     const int64_t nchunk = g.interior_bytes / 16;
-    for (int64_t ch0 = 0; ch0 < nchunk; ch0 += NCT) {
-        const int64_t ch = ch0 + tid;
+    const uint4* base = reinterpret_cast<const uint4*>(g.interior);
+    for (int64_t ch0 = 0; ch0 < nchunk; ch0 += (int64_t)NCT * RUN) {
+      uint4 vr[RUN];
+#pragma unroll
+      for (int u = 0; u < RUN; ++u) {
+          const int64_t ch = ch0 + tid + (int64_t)u * NCT;
+          vr[u] = ch < nchunk ? __ldg(base + ch) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < RUN; ++u) {
+        const int64_t ch = ch0 + tid + (int64_t)u * NCT;
         const bool valid = ch < nchunk;
         float x[VEC];
         int c0 = 0;
         if (valid) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(g.interior) + ch);
+            const uint4 v = vr[u];
             E::unpack(v, x);
             c0 = g.head + (int)(ch * VEC);
             if (p.pen) {
@@ -411,6 +488,7 @@ __device__ __forceinline__ void for_row(const KParams& P, const Smem& s, const R
         }
 #pragma unroll
         for (int e = 0; e < VEC; ++e) f(valid, c0 + e, x[e]);
+      }
     }
 }
 
@@ -442,7 +520,7 @@ struct Located {
 };
 
 template <int DT>
-__device__ Located locate(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g, int tid,
+__device__ __forceinline__ Located locate(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g, int tid,
                           uint32_t rlo, uint32_t rhi, float ylo, float yhi, uint64_t target, float My, float scale,
                           uint32_t slot0) {
     const int lane = tid & 31;
@@ -565,6 +643,304 @@ __device__ Located locate(const KParams& P, const Smem& s, const RowParams& p, i
     return L;
 }
 
+// ---------------------------------------------------------------------------
+// Windowed locate: locate()'s contract at a fraction of its cost.
+//
+// It works on x (the penalised logit before temperature): y = x / T is
+// monotone in x, so every region and window test is two float compares, and
+// the exact division is only done for the few collected elements.
+//   * A histogram pass only COUNTS elements per bin (one 32-bit shared atomic
+//     each). NW bins are linear in x over the current window.
+//   * A bin's mass lies between count * m(lower edge) and count * m(upper
+//     edge); the edges are widened by the rounding slack of the bin function
+//     and of y = x / T, and m by the error of the fast exponentials and of the
+//     rounding to integers. The bins whose bracketed cumulative masses
+//     straddle the target make the next window, which certainly holds the
+//     crossing element. Window edges are closed under equal y, so a run of
+//     tied values is never split.
+//   * The mass above the window is summed exactly in registers, from
+//     2^(x * log2e / T - My * log2e).
+//   * When the window fits the free buffer its elements are collected with
+//     their y-keys and the crossing element is selected exactly, with the
+//     integer masses locate() gives elements of the candidate buffer.
+// `fallback` is set when no window fits (a run of equal values longer than
+// the free space) or a bracket is found violated.
+// ---------------------------------------------------------------------------
+constexpr int NW = 4 * NB;   // bins per level; the counts use the blo/bhi area (4 * NB words)
+constexpr int WDEPTH = 3;    // histogram levels before the fallback
+
+__device__ __forceinline__ int wbin(float x, float xa, float inv) {
+    const float t = (x - xa) * inv;
+    if (!(t > 0.0f)) return 0;
+    return t >= (float)(NW - 1) ? NW - 1 : (int)t;
+}
+
+struct WWin {
+    int lo, hi;
+    uint32_t count;
+    bool any;
+};
+
+// One level: bins over [wl, wu] (x), counts in cnt. Returns the bins whose
+// bracketed cumulative mass, descending from `above`, straddles T.
+__device__ WWin wscan(const Smem& s, const uint32_t* cnt, float wl, float wu, float inv, double sx,
+                      const RowParams& p, float My, double scale, double above, double T, int tid) {
+    constexpr int PER = NW / NCT;
+    const int lane = tid & 31, wid = tid >> 5;
+    const double w = inv > 0.0f ? 1.0 / (double)inv : 0.0;
+    const double rT = p.temp_on ? 1.0 / (double)p.T : 1.0;
+    double lq[PER], uq[PER];
+    uint32_t c[PER];
+    double sl = 0.0, su = 0.0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int b = NW - 1 - (tid * PER + j);   // thread order = descending bins
+        c[j] = cnt[b];
+        lq[j] = 0.0;
+        uq[j] = 0.0;
+        if (c[j]) {
+            double e0 = (b == 0 || w == 0.0) ? (double)wl : (double)wl + (double)b * w - sx;
+            double e1 = (b == NW - 1 || w == 0.0) ? (double)wu : (double)wl + (double)(b + 1) * w + sx;
+            e0 = fmax(e0, (double)wl) * rT;
+            e1 = fmin(e1, (double)wu) * rT;
+            e0 -= fabs(e0) * 2.4e-7;   // y = fl(x / T)
+            e1 += fabs(e1) * 2.4e-7;
+            const double ml = floor(exp(e0 - (double)My) * scale * (1.0 - 3e-5)) - 1.0;
+            const double mh = fmin(ceil(exp(e1 - (double)My) * scale * (1.0 + 3e-5)) + 1.0, 1e300);
+            lq[j] = (double)c[j] * fmax(ml, 0.0);
+            uq[j] = (double)c[j] * mh;
+        }
+        sl += lq[j];
+        su += uq[j];
+    }
+    double il = sl, iu = su;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double tl = __shfl_up_sync(0xffffffffu, il, o);
+        const double tu = __shfl_up_sync(0xffffffffu, iu, o);
+        if (lane >= o) { il += tl; iu += tu; }
+    }
+    if (lane == 31) { s.redd[wid] = il; s.red64[wid] = (uint64_t)__double_as_longlong(iu); }
+    csync();
+    double bl = 0.0, bu = 0.0;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i)
+        if (i < wid) { bl += s.redd[i]; bu += __longlong_as_double((long long)s.red64[i]); }
+    csync();
+    double pl = bl + il - sl, pu = bu + iu - su;
+    int bmax = -1, bmin = NW;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int b = NW - 1 - (tid * PER + j);
+        const double exL = (above + pl) * (1.0 - 1e-12) - 2.0;
+        const double inU = (above + pu + uq[j]) * (1.0 + 1e-12) + 2.0;
+        if (c[j] && exL <= T && T < inU) { bmax = max(bmax, b); bmin = min(bmin, b); }
+        pl += lq[j];
+        pu += uq[j];
+    }
+    WWin out;
+    const uint32_t hi1 = cons_max_u32((uint32_t)(bmax + 1), s, tid);
+    const uint32_t lo = cons_min_u32((uint32_t)bmin, s, tid);
+    out.any = hi1 > 0u;
+    out.hi = (int)hi1 - 1;
+    out.lo = (int)lo;
+    uint64_t cc = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int b = NW - 1 - (tid * PER + j);
+        if (out.any && b >= out.lo && b <= out.hi) cc += c[j];
+    }
+    out.count = (uint32_t)cons_sum_u64(cc, s, tid);
+    return out;
+}
+
+// Exact mass of region R (y-keys in [rlo, rhi]), one row pass.
+template <int DT>
+__device__ __forceinline__ uint64_t region_mass(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g,
+                                int tid, uint32_t rlo, uint32_t rhi, float My, float scale) {
+    uint64_t acc = 0;
+    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+        const float y = ydiv(p, x);
+        const uint32_t k = fkey(y);
+        if (valid && k >= rlo && k <= rhi) acc += q_of(efast(y, My), scale);
+    });
+    return cons_sum_u64(acc, s, tid);
+}
+
+struct WLoc {
+    bool fallback;
+    Located L;
+};
+
+template <int DT>
+__device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g, int tid,
+                        uint32_t rlo, uint32_t rhi, float ylo, float yhi, uint64_t target, float My, float scale,
+                        uint32_t slot0) {
+    WLoc W;
+    Located& L = W.L;
+    W.fallback = false;
+    L.ok = false; L.in_buffer = false; L.key = 0u; L.before = 0; L.at = 0; L.n_at = 0; L.total = 0;
+    L.n0 = slot0; L.n1 = slot0;
+    if (rlo > rhi) return W;
+    const uint32_t room = slot0 < (uint32_t)CAND_CAP ? (uint32_t)CAND_CAP - slot0 : 0u;
+    const uint32_t fit = room - room / 8u;   // margin for the edge slack and tie closure
+    uint32_t* cnt = s.blo;                   // NW words (blo and bhi are contiguous)
+    // region in x; below `cutoff` under the maximum a mass rounds to 0 at scale 2^S
+    const float cutoff = (float)(P.mass_shift + 2) * 0.6931472f;
+    // the region's top is its largest y (yhi), so the window stays finite
+    const float xlo = x_lower(p, rlo), xhi = x_upper(p, min(rhi, fkey(yhi)));
+    const float xpos = x_lower(p, fkey(fmaxf(ylo, My - cutoff)));
+    float wl = fmaxf(xlo, xpos), wu = xhi;   // current window (nested, closed under equal y)
+    if (!(wu >= wl)) return W;               // every mass in R rounds to 0: total 0
+    const float cx = L2E / p.T;              // m(x) = 2^(x * cx + nmy), cx == L2E when T == 1
+    const float nmy = -(My * L2E);
+    const float cxx = p.temp_on ? cx : L2E;
+    const double sc = (double)scale;
+    const double T = (double)target;
+    uint64_t above = 0;
+    bool beyond = false;
+    for (int d = 0;; ++d) {
+        const float span = wu - wl;
+        float inv = span > 0.0f ? (float)NW / span : 0.0f;
+        if (!(inv < INFINITY)) inv = 0.0f;
+        const double sx = 1e-6 * (double)span;
+        for (int i = tid; i < NW; i += NCT) cnt[i] = 0u;
+        csync();
+        uint64_t acc = 0;
+        const float a0 = wl, a1 = wu, bi = inv;
+        for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+            if (!valid || !(x >= xlo && x <= xhi)) return;
+            if (x > a1) acc += q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+            else if (x >= a0) atomicAdd(&cnt[wbin(x, a0, bi)], 1u);
+        });
+        csync();
+        if (d > 0) above = cons_sum_u64(acc, s, tid);
+        const WWin win = wscan(s, cnt, wl, wu, inv, sx, p, My, sc, (double)above, T, tid);
+        if (!win.any) { beyond = true; break; }
+        // the window's x-range, widened by the slack, closed under equal y
+        const double w = inv > 0.0f ? 1.0 / (double)inv : 0.0;
+        float nl = wl, nu = wu;
+        if (w > 0.0) {
+            if (win.lo > 0) nl = __double2float_rd((double)wl + (double)win.lo * w - sx);
+            if (win.hi < NW - 1) nu = __double2float_ru((double)wl + (double)(win.hi + 1) * w + sx);
+        }
+        nl = fmaxf(wl, x_lower(p, fkey(ydiv(p, nl))));
+        nu = fminf(wu, x_upper(p, fkey(ydiv(p, nu))));
+        const bool progress = nl > wl || nu < wu;
+        wl = nl;
+        wu = nu;
+        if (win.count <= fit) break;
+        if (d + 1 >= WDEPTH || !progress) {
+            W.fallback = true;
+            return W;
+        }
+    }
+    if (beyond) {
+        // the target lies at or past the region's total mass
+        L.total = region_mass<DT>(P, s, p, r, g, tid, rlo, rhi, My, scale);
+        return W;
+    }
+    // ---- collect the window [wl, wu]; exact mass above it ----
+    if (tid == 0) s.ctl->ncol = 0u;
+    csync();
+    const int lane = tid & 31;
+    uint64_t accA = 0;
+    uint32_t kmn = 0xffffffffu, kmx = 0u;
+    const float a0 = wl, a1 = wu;
+    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+        const bool inr = valid && x >= xlo && x <= xhi;
+        const bool in = inr && x >= a0 && x <= a1;
+        if (inr && x > a1) accA += q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+        const uint32_t bal = __ballot_sync(0xffffffffu, in);
+        if (bal) {
+            const int lead = __ffs(bal) - 1;
+            uint32_t b0 = 0u;
+            if (lane == lead) b0 = atomicAdd(&s.ctl->ncol, (uint32_t)__popc(bal));
+            b0 = __shfl_sync(0xffffffffu, b0, lead);
+            if (in) {
+                const uint32_t k = fkey(ydiv(p, x));
+                const uint32_t pos = slot0 + b0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
+                if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = k; s.cid[pos] = (uint32_t)c; }
+                kmn = min(kmn, k);
+                kmx = max(kmx, k);
+            }
+        }
+    });
+    const uint64_t A = cons_sum_u64(accA, s, tid);
+    kmn = cons_min_u32(kmn, s, tid);
+    kmx = cons_max_u32(kmx, s, tid);
+    const uint32_t ncol = s.ctl->ncol;
+    if (ncol > room) { W.fallback = true; return W; }
+    const uint32_t n1 = slot0 + ncol;
+    uint64_t wloc = 0;
+    for (uint32_t i = slot0 + tid; i < n1; i += NCT) wloc += q_of(efast(funkey(s.ckey[i]), My), scale);
+    const uint64_t Wm = cons_sum_u64(wloc, s, tid);
+    if (target < A) { W.fallback = true; return W; }   // bracket violated: take the exact path
+    if (target >= A + Wm) {
+        // past the window: only when the target is past the region's total
+        L.total = region_mass<DT>(P, s, p, r, g, tid, rlo, rhi, My, scale);
+        if (target < L.total) W.fallback = true;
+        return W;
+    }
+    const SelOut so = block_select<true, false>(
+        [&](auto&& f) {
+            for (uint32_t i0 = slot0; i0 < n1; i0 += NCT) {
+                const uint32_t i = i0 + tid;
+                const bool v = i < n1;
+                const uint32_t k = v ? s.ckey[i] : 0u;
+                f(v, k, v ? q_of(efast(funkey(k), My), scale) : 0ull);
+            }
+        },
+        target - A, kmn, varying_bits(kmn, kmx), s, tid);
+    L.ok = so.ok; L.in_buffer = true; L.key = so.key; L.before = A + so.before; L.at = so.at; L.n_at = so.n_at;
+    L.n0 = slot0; L.n1 = n1;
+    L.total = A + Wm;   // mass at and above the window (the part below is not needed)
+    if (!so.ok) W.fallback = true;
+    return W;
+}
+
+// Cold entry points of the multi-pass paths. They take only the kernel
+// parameters (grid constant), the row and scalars, and rebuild the shared
+// memory carve, row parameters and geometry themselves: no struct of the
+// streaming loop has its address taken, so it stays in registers.
+template <int DT>
+__device__ __noinline__ WLoc wlocate_cold(const KParams& P, int tid, int r, uint32_t rlo, uint32_t rhi, float ylo,
+                                          float yhi, uint64_t target, float My, float scale, uint32_t slot0) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    return wlocate<DT>(P, s, p, r, g, tid, rlo, rhi, ylo, yhi, target, My, scale, slot0);
+}
+template <int DT>
+__device__ __noinline__ Located locate_cold(const KParams& P, int tid, int r, uint32_t rlo, uint32_t rhi, float ylo,
+                                            float yhi, uint64_t target, float My, float scale, uint32_t slot0) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    return locate<DT>(P, s, p, r, g, tid, rlo, rhi, ylo, yhi, target, My, scale, slot0);
+}
+template <int DT>
+__device__ __noinline__ uint64_t region_mass_cold(const KParams& P, int tid, int r, uint32_t rlo, uint32_t rhi,
+                                                  float My, float scale) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    return region_mass<DT>(P, s, p, r, g, tid, rlo, rhi, My, scale);
+}
+
+template <int DT>
+__device__ __forceinline__ Located locate_fast(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g,
+                               int tid, uint32_t rlo, uint32_t rhi, float ylo, float yhi, uint64_t target, float My,
+                               float scale, uint32_t slot0, bool clamp) {
+    (void)s; (void)p; (void)g;
+    WLoc w = wlocate_cold<DT>(P, tid, r, rlo, rhi, ylo, yhi, target, My, scale, slot0);
+    // like locate(), a clamped call answers a target past the total with the last element
+    if (clamp && !w.fallback && !w.L.ok && w.L.total > 0 && target >= w.L.total)
+        w = wlocate_cold<DT>(P, tid, r, rlo, rhi, ylo, yhi, w.L.total - 1, My, scale, slot0);
+    if (!w.fallback) return w.L;
+    return locate_cold<DT>(P, tid, r, rlo, rhi, ylo, yhi, target, My, scale, slot0);
+}
+
 // j-th smallest column (0-based) among entries [i0, i1) with key k.
 __device__ __forceinline__ uint32_t jth_id(const KParams& P, const Smem& s, int tid, uint32_t i0, uint32_t i1,
                                            uint32_t k, uint32_t n_at, uint64_t j) {
@@ -605,42 +981,74 @@ __device__ uint32_t jth_id_row(const KParams& P, const Smem& s, const RowParams&
 template <int DT>
 __device__ void producer(const KParams& P, const Smem& s) {
     constexpr int ESZ = Elem<DT>::SIZE;
+    constexpr int HEAVY = 1 << 30;   // queue entry flag: the row may be re-read after its stream
     volatile int* abort = &s.ctl->abort;
     const uint32_t ns = (uint32_t)P.nstage;
+    const unsigned B = (unsigned)P.batch;
     uint32_t it = 0, k = 0, st = 0, ph = 0;
+    int held[ROW_CLAIM];
+    int nheld = 0, hpos = 0;
+    const uint64_t pol_keep = l2_policy_evict_last();
+    // next owned queue entry (row | HEAVY), -1 when the queue is exhausted
     auto fetch = [&]() -> int {
-        const unsigned v = atomicAdd(&P.ws->next_row, 1u);
-        return v < (unsigned)P.batch ? (int)v : -1;
+        while (hpos == nheld) {
+            const unsigned v = atomicAdd(&P.ws->next_row, (unsigned)ROW_CLAIM);
+            if (v >= 2u * B) return -1;
+            bool hv[ROW_CLAIM];
+#pragma unroll
+            for (int i = 0; i < ROW_CLAIM; ++i) hv[i] = (v + i < 2u * B) && row_heavy(P, (int)((v + i) % B));
+            nheld = 0; hpos = 0;
+#pragma unroll
+            for (int i = 0; i < ROW_CLAIM; ++i) {
+                const unsigned u = v + (unsigned)i;
+                if (u < 2u * B && (u < B) == hv[i]) held[nheld++] = (int)(u % B) | (hv[i] ? HEAVY : 0);
+            }
+        }
+        return held[hpos++];
     };
     auto drain = [&]() {
         const uint32_t first = it > ns ? it - ns : 0u;
         for (uint32_t j = first; j < it; ++j) mbar_wait_for(&s.full[j % ns], (j / ns) & 1u, WAIT_LIMIT_NS);
     };
-    auto give_up = [&](int rr) {
+    auto mark = [&](int e) {
+        if (e < 0) return;
+        const int rr = e & (HEAVY - 1);
+        P.out_ids[rr] = -1;
+        if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT;
+    };
+    auto give_up = [&](int e) {
         *abort = 1;
-        if (rr >= 0) { P.out_ids[rr] = -1; if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT; }
+        mark(e);
+        while (hpos < nheld) mark(held[hpos++]);   // claimed, never published
         drain();
     };
-    int r = fetch();
+    int e = fetch();
     while (true) {
         const uint32_t slot = k % RQ, rph = (k / RQ) & 1u;
-        if (!mbar_wait(&s.rowempty[slot], rph ^ 1u, abort)) { give_up(r); return; }
-        s.ctl->rowq[slot] = r;
+        if (!mbar_wait(&s.rowempty[slot], rph ^ 1u, abort)) { give_up(e); return; }
+        s.ctl->rowq[slot] = e < 0 ? -1 : (e & (HEAVY - 1));
         mbar_arrive(&s.rowfull[slot]);
         ++k;
-        if (r < 0) return;
-        const int rcur = r;
-        r = fetch();  // next row index, fetched while this row streams
+        if (e < 0) return;
+        const int rcur = e & (HEAVY - 1);
+        // rows that may be re-read after the stream stay in L2 until the
+        // consumers release them (sample_row returns them to normal priority)
+        const bool keep = (e & HEAVY) != 0;
         const RowGeom g = row_geom<ESZ>(P, rcur);
+        int en = -2;   // next entry, looked up once the ring is full
         for (int t = 0; t < g.ntiles; ++t, ++it) {
-            if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) { give_up(r); return; }
+            if (en == -2 && !mbar_test(&s.empty[st], ph ^ 1u)) en = fetch();
+            if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) { give_up(en); return; }
             const int64_t off = (int64_t)t * TILE_BYTES;
             const int64_t left = g.interior_bytes - off;
             const uint32_t bytes = (uint32_t)(left < TILE_BYTES ? left : TILE_BYTES);
             mbar_arrive_expect_tx(&s.full[st], bytes);
-            bulk_g2s(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st]);
+            if (keep) bulk_g2s_hint(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st], pol_keep);
+            else bulk_g2s(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st]);
             if (++st == ns) { st = 0; ph ^= 1u; }
         }
+        if (en == -2) en = fetch();
+        e = en;
     }
 }
 
@@ -649,193 +1057,18 @@ __device__ void producer(const KParams& P, const Smem& s) {
 // ---------------------------------------------------------------------------
 struct RingPos { uint32_t st, ph; };
 
+// ---------------------------------------------------------------------------
+// After the stream: row statistics, the decision (greedy / sampling), outputs.
+// ---------------------------------------------------------------------------
 template <int DT>
-__device__ void sample_row(const KParams& P, const Smem& s, const int tid, const int r, RingPos& rp) {
+__device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, const int tid, const int r, const RowParams& p,
+                                        const RowGeom& g, const Stream& st, const bool aborted) {
     using E = Elem<DT>;
     constexpr int ESZ = E::SIZE, VEC = E::VEC;
-    const int lane = tid & 31, warp = tid >> 5;
+    (void)ESZ;
     RowCtl* ctl = s.ctl;
     volatile int* abort = &ctl->abort;
-    const uint32_t ns = (uint32_t)P.nstage;
     const float scale = __uint_as_float((uint32_t)(127 + P.mass_shift) << 23);  // 2^S
-    const RowParams p = row_params(P, r);
-    const RowGeom g = row_geom<ESZ>(P, r);
-    if (tid == 0) {
-        ctl->wcnt[0] = ctl->wcnt[1] = ctl->wcnt[2] = 0u;
-        ctl->ovf[0] = ctl->ovf[1] = ctl->ovf[2] = 0;
-        ctl->hikey = 0u; ctl->lokey = 0xffffffffu; ctl->xmin = -INFINITY;
-        ctl->status = p.bad; ctl->nunique = 0u;
-    }
-    csync();
-    if (p.pen) history_prologue(P, s, p, r, tid);
-    const uint32_t U = p.pen ? ctl->nunique : 0u;
-    Stream st;
-    st.tmax = -INFINITY; st.imax = -INFINITY; st.itile = -1; st.tmin = INFINITY;
-    st.zm = -1e30f; st.nzmc = -(st.zm * p.c); st.z0 = 0.0f; st.z1 = 0.0f;
-    st.xmin = -INFINITY; st.cand = p.cand; st.base = 0; st.win = 0;
-    st.bestv = -INFINITY; st.bestc = 0xffffffffu;
-    st.khi = 0u; st.klo = 0xffffffffu;
-    const uint8_t* rowp = reinterpret_cast<const uint8_t*>(P.logits) + (int64_t)r * P.row_stride * ESZ;
-
-    // ---- streamed interior ----
-    for (int t = 0; t < g.ntiles; ++t) {
-        const bool ok = mbar_wait(&s.full[rp.st], rp.ph, abort);
-        if (!ok) *abort = 1;
-        const uint8_t* tile = s.ring + (int64_t)rp.st * TILE_BYTES;
-        const int64_t left = g.interior_bytes - (int64_t)t * TILE_BYTES;
-        const int nch = ok ? (int)((left < TILE_BYTES ? left : TILE_BYTES) / 16) : 0;
-        const int tcol0 = g.head + t * (TILE_BYTES / ESZ);
-        uint4 v[CPT];
-#pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-            const int ch = tid + j * NCT;
-            if (ch < nch) v[j] = *reinterpret_cast<const uint4*>(tile + ch * 16);
-            else v[j] = make_uint4(Neg<DT>::W, Neg<DT>::W, Neg<DT>::W, Neg<DT>::W);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s.empty[rp.st]);   // the stage now lives in registers
-        if (++rp.st == ns) { rp.st = 0; rp.ph ^= 1u; }
-        uint32_t hb[CPT];
-#pragma unroll
-        for (int j = 0; j < CPT; ++j) hb[j] = 0u;
-        if (p.pen) {
-#pragma unroll
-            for (int j = 0; j < CPT; ++j) {
-                const int ch = tid + j * NCT;
-                if (ch < nch) {
-                    const int c0 = tcol0 + ch * VEC;
-                    uint32_t bits = hist_bits(s, P.nwords, c0, VEC);
-                    hb[j] = bits;
-                    while (bits) {
-                        const int e = __ffs(bits) - 1;
-                        bits &= bits - 1;
-                        const uint32_t rk = hist_rank(s, (uint32_t)(c0 + e));
-                        if (rk < U) s.sval[rk] = elem_get<DT>(v[j], e);
-                        elem_mask<DT>(v[j], e);
-                    }
-                }
-            }
-        }
-        const float m = chunks_max<DT>(v);
-        st.tmax = fmax_nan(st.tmax, m);
-        if (p.mode == MODE_GREEDY && m > st.imax) { st.imax = m; st.itile = t; }
-        if (p.zsum) {
-            st.tmin = fminf(st.tmin, chunks_min<DT>(v));
-            if (m > st.zm) {
-                const float nn = -(m * p.c);
-                const float f = ex2_approx(nn - st.nzmc);
-                st.z0 *= f; st.z1 *= f;
-                st.zm = m; st.nzmc = nn;
-            }
-            chunks_sumexp<DT>(v, p.c, st.nzmc, st.z0, st.z1);
-        }
-        if (st.cand) {
-            if (t == 0) {
-                // starting threshold from the first tile: the K-th largest of
-                // disjoint group maxima (thread maxima for K <= NCT/2, chunk
-                // maxima for K <= NCT, elements otherwise) bounds the row's K-th
-                // largest from below
-                float cm[CPT];
-#pragma unroll
-                for (int j = 0; j < CPT; ++j) cm[j] = chunk_max1<DT>(v[j]);
-                const int K = p.K;
-                // key range of the values the select will see
-                float lo_v = INFINITY;
-                if (K <= NCT / 2) lo_v = m;
-                else if (K <= NCT) { for (int j = 0; j < CPT; ++j) lo_v = fminf(lo_v, cm[j]); }
-                else lo_v = chunks_min<DT>(v);
-                const uint32_t klo = cons_min_u32((lo_v == lo_v && lo_v > -INFINITY) ? fkey(lo_v) : 0xffffffffu, s, tid);
-                const uint32_t khi = cons_max_u32((m == m && m > -INFINITY) ? fkey(m) : 0u, s, tid);
-                const SelOut so = block_select<true, true>(
-                    [&](auto&& f) {
-                        if (K <= NCT / 2) {
-                            f(m == m && m > -INFINITY, fkey(m), 1ull);
-                        } else if (K <= NCT) {
-#pragma unroll
-                            for (int j = 0; j < CPT; ++j) f(cm[j] == cm[j] && cm[j] > -INFINITY, fkey(cm[j]), 1ull);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < CPT; ++j)
-#pragma unroll
-                                for (int e = 0; e < VEC; ++e) {
-                                    const float x = elem_get<DT>(v[j], e);
-                                    f(x == x && x > -INFINITY, fkey(x), 1ull);
-                                }
-                        }
-                    },
-                    (uint64_t)(K - 1), klo <= khi ? klo : 0u, klo <= khi ? varying_bits(klo, khi) : 32, s, tid);
-                if (so.ok && tid == 0) {
-                    const float xm = xmin_for(p, funkey(so.key));
-                    if (xm > ctl->xmin) ctl->xmin = xm;
-                }
-                csync();
-                st.xmin = ctl->xmin;
-            }
-            uint32_t pick = 0;
-            if (m >= st.xmin) {
-#pragma unroll
-                for (int j = 0; j < CPT; ++j) {
-                    const int ch = tid + j * NCT;
-                    if (ch < nch) {
-#pragma unroll
-                        for (int e = 0; e < VEC; ++e)
-                            if (!((hb[j] >> e) & 1u) && elem_get<DT>(v[j], e) >= st.xmin) pick |= 1u << (j * VEC + e);
-                    }
-                }
-            }
-            while (pick) {
-                const int i = __ffs(pick) - 1;
-                pick &= pick - 1;
-                const int j = i / VEC, e = i % VEC;
-                uint4 vv = v[0];
-#pragma unroll
-                for (int jj = 1; jj < CPT; ++jj) if (jj == j) vv = v[jj];
-                append1(s, st, fkey(elem_get<DT>(vv, e)), (uint32_t)(tcol0 + (tid + j * NCT) * VEC + e));
-            }
-            // appends per tile fall off as 1/t: check every tile early in the
-            // row, every 2nd and then every 4th tile later (appends are bounds
-            // checked, an overflow sends the row to the multi-pass path)
-            const bool chk = t < 8 || (t < 16 ? (t & 1) == 1 : (t & 3) == 3) || t == g.ntiles - 1;
-            if (chk) window_check(p, s, tid, st, (uint32_t)HWM);
-        }
-    }
-
-    // ---- ragged head/tail columns (at most 2 * (VEC - 1)), one per lane of warp 0;
-    //      processed after the interior so the candidate filter is final ----
-    if (warp == 0) {
-        const int nh = g.head, nt = P.vocab - g.tail0;
-        bool valid = lane < nh + nt;
-        const int c = lane < nh ? lane : g.tail0 + (lane - nh);
-        float x = -INFINITY;
-        if (valid) {
-            x = E::load(rowp, c);
-            if (p.pen && (hist_bits(s, P.nwords, c, 1) & 1u)) {
-                const uint32_t rk = hist_rank(s, (uint32_t)c);
-                if (rk < U) s.sval[rk] = x;   // merged after the stream
-                valid = false;
-            }
-        }
-        process_one(p, s, st, x, (uint32_t)(valid ? c : 0), valid, lane);
-    }
-
-    // ---- merge the history columns with their penalised values ----
-    if (p.pen) {
-        csync();
-        for (uint32_t i0 = 0; i0 < U; i0 += NCT) {
-            const uint32_t i = i0 + tid;
-            const bool valid = i < U;
-            float x = -INFINITY;
-            uint32_t col = 0;
-            if (valid) { col = s.scol[i]; x = penalize(p, s, i, s.sval[i]); }
-            process_one(p, s, st, x, col, valid, lane);
-        }
-    }
-    if (st.cand) window_check(p, s, tid, st, (uint32_t)HWM + (CAND_CAP - HWM) / 2);
-    // uniform snapshot of the abort flag (the producer may set it at any time)
-    if (tid == 0) ctl->snap = (*abort != 0) ? 1u : 0u;
-    csync();
-    const bool aborted = ctl->snap != 0;
-
     // ---- row statistics ----
     const float M = cons_max_nan(st.tmax, s, tid);
     int status = ctl->status;
@@ -954,8 +1187,7 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
             double Qn;
             if (p.mode == MODE_TOPK && cand_ok) Qn = (double)AC;
             else if (p.mode == MODE_TOPK) {
-                const Located L0 = locate<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, 0ull, My, scale, 0u);
-                Qn = (double)L0.total;
+                Qn = (double)region_mass_cold<DT>(P, tid, r, rlo, rhi, My, scale);
             } else Qn = Zq;
             const double Pd = (double)p.top_p * Qn;
             const uint64_t Pt = (uint64_t)floor(Pd);
@@ -979,7 +1211,7 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
             } else {
                 status |= FG_ROW_GENERAL_PATH;
                 const uint64_t tr = Pt >= AC ? Pt - AC : 0ull;
-                const Located L = locate<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, tr, My, scale, nC);
+                const Located L = locate_fast<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, tr, My, scale, nC, false);
                 if (!L.ok || tr >= L.total) {
                     cut = false;               // the cut lies below every element: keep all
                     Qf = AC + L.total;
@@ -995,8 +1227,7 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
         } else {
             if (p.mode == MODE_TOPK && cand_ok) Qf = AC;
             else if (p.mode == MODE_TOPK) {
-                const Located L0 = locate<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, 0ull, My, scale, 0u);
-                Qf = L0.total;
+                Qf = region_mass_cold<DT>(P, tid, r, rlo, rhi, My, scale);
             } else Qf = (uint64_t)Zq;   // unfiltered: every token kept
         }
         // ---- inverse-CDF draw in descending-probability order ----
@@ -1025,7 +1256,7 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
                 const uint64_t t2 = target - (nC > 0 ? AC : 0ull);
                 const uint32_t rlo2 = cut_in_R ? tstar : rlo;
                 const float ylo2 = cut_in_R ? fmaxf(funkey(tstar), My - 64.0f) : yRlo;
-                const Located L = locate<DT>(P, s, p, r, g, tid, rlo2, rhi, ylo2, yRhi, t2, My, scale, nC);
+                const Located L = locate_fast<DT>(P, s, p, r, g, tid, rlo2, rhi, ylo2, yRhi, t2, My, scale, nC, true);
                 if (L.ok) {
                     const uint64_t qd = L.n_at ? L.at / L.n_at : 0;
                     uint64_t j = qd ? (t2 - L.before) / qd : 0;
@@ -1086,31 +1317,391 @@ __device__ void sample_row(const KParams& P, const Smem& s, const int tid, const
     if (aborted && tid == 0) *abort = 1;
 }
 
+// Starting threshold of the candidate filter from the first tile (cold: once
+// per row). Takes the thread's two chunks by value.
 template <int DT>
-__device__ void consumer(const KParams& P, const Smem& s, const int tid) {
+__device__ __forceinline__ void tau0_cold(const KParams& P, int tid, int r, uint4 v0, uint4 v1, float m) {
+    static_assert(CPT == 2, "tau0_cold takes CPT chunks by value");
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    RowCtl* ctl = s.ctl;
+    constexpr int VEC = Elem<DT>::VEC;
+    const uint4 v[CPT] = {v0, v1};
+    // starting threshold from the first tile: the K-th largest of
+    // disjoint group maxima (thread maxima for K <= NCT/2, chunk
+    // maxima for K <= NCT, elements otherwise) bounds the row's K-th
+    // largest from below
+    float cm[CPT];
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) cm[j] = chunk_max1<DT>(v[j]);
+    const int K = p.K;
+    // key range of the values the select will see
+    float lo_v = INFINITY;
+    if (K <= NCT / 2) lo_v = m;
+    else if (K <= NCT) { for (int j = 0; j < CPT; ++j) lo_v = fminf(lo_v, cm[j]); }
+    else lo_v = chunks_min<DT>(v);
+    const uint32_t klo = cons_min_u32((lo_v == lo_v && lo_v > -INFINITY) ? fkey(lo_v) : 0xffffffffu, s, tid);
+    const uint32_t khi = cons_max_u32((m == m && m > -INFINITY) ? fkey(m) : 0u, s, tid);
+    const SelOut so = block_select<true, true>(
+        [&](auto&& f) {
+            if (K <= NCT / 2) {
+                f(m == m && m > -INFINITY, fkey(m), 1ull);
+            } else if (K <= NCT) {
+#pragma unroll
+                for (int j = 0; j < CPT; ++j) f(cm[j] == cm[j] && cm[j] > -INFINITY, fkey(cm[j]), 1ull);
+            } else {
+#pragma unroll
+                for (int j = 0; j < CPT; ++j)
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        const float x = elem_get<DT>(v[j], e);
+                        f(x == x && x > -INFINITY, fkey(x), 1ull);
+                    }
+            }
+        },
+        (uint64_t)(K - 1), klo <= khi ? klo : 0u, klo <= khi ? varying_bits(klo, khi) : 32, s, tid);
+    if (so.ok && tid == 0) {
+        const float xm = xmin_for(p, funkey(so.key));
+        if (xm > ctl->xmin) ctl->xmin = xm;
+    }
+    csync();
+}
+
+__device__ __forceinline__ void history_prologue_cold(const KParams& P, int tid, int r) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    history_prologue(P, s, p, r, tid);
+}
+
+template <int DT>
+__device__ __forceinline__ void finish_row_cold(const KParams& P, int tid, int r, float tmax, float tmin, float z0,
+                                             float z1, float nzmc, bool cand, uint32_t base, float imax, int itile,
+                                             float bestv, uint32_t bestc, bool aborted) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    Stream st;
+    st.tmax = tmax; st.tmin = tmin; st.z0 = z0; st.z1 = z1; st.nzmc = nzmc; st.zm = 0.0f; st.xmin = 0.0f;
+    st.cand = cand; st.base = base; st.imax = imax; st.itile = itile; st.bestv = bestv; st.bestc = bestc;
+    st.win = 0u; st.khi = 0u; st.klo = 0u;
+    finish_row<DT>(P, s, tid, r, p, g, st, aborted);
+}
+
+// The streamed interior of one row: every tile of the ring through the
+// history mask, max, sum-exp and candidate filter. Kept out of line, with only
+// its own state live, so that the loop has the whole register budget; the
+// stream state and ring position are copied in and written back once.
+// Window schedule of the candidate filter within a row.
+struct TileCtx {
+    int last_chk, next_chk;   // tile of the last window end, tile of the next
+    int span;                 // tiles in the window that just ended
+    uint64_t rate2;           // twice the appends of that window
+};
+
+// One streamed tile: history mask, max, sum-exp, candidate filter, window
+// end. Returns true when a compaction is due (run by the caller, outside the
+// streaming loop). FIRST: tile 0, which also sets the starting threshold.
+template <int DT, bool FIRST>
+__device__ __forceinline__ bool process_tile(const KParams& P, const RowParams& p, const RowGeom& g, const int tid,
+                                             const int r, const int t, RingPos& rp, Stream& st, const uint32_t U,
+                                             TileCtx& tc) {
+    using E = Elem<DT>;
+    constexpr int ESZ = E::SIZE, VEC = E::VEC;
+    constexpr uint32_t O_ABORT = (uint32_t)offsetof(RowCtl, abort);
+    constexpr uint32_t O_XMIN = (uint32_t)offsetof(RowCtl, xmin);
+    constexpr uint32_t O_WCNT = (uint32_t)offsetof(RowCtl, wcnt);
+    constexpr uint32_t O_OVF = (uint32_t)offsetof(RowCtl, ovf);
+    const int lane = tid & 31;
+    const uint32_t ns = (uint32_t)P.nstage;
+    // shared-window addresses: symbol + grid-constant offsets, nothing held
+    const uint32_t sb = smem_base32();
+    const uint32_t a_ctl = sb + (uint32_t)P.off_ctl;
+    const bool ok = mbar_wait_a(sb + 8u * rp.st, rp.ph, a_ctl + O_ABORT);
+    if (!ok) sts_u32(a_ctl + O_ABORT, 1u);
+    const uint32_t tile = sb + (uint32_t)P.off_ring + rp.st * (uint32_t)TILE_BYTES;
+    const int64_t left = g.interior_bytes - (int64_t)t * TILE_BYTES;
+    const int nch = ok ? (int)((left < TILE_BYTES ? left : TILE_BYTES) / 16) : 0;
+    const int tcol0 = g.head + t * (TILE_BYTES / ESZ);
+    uint4 v[CPT];
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+        const int ch = tid + j * NCT;
+        if (ch < nch) v[j] = lds_v4(tile + (uint32_t)ch * 16u);
+        else v[j] = make_uint4(Neg<DT>::W, Neg<DT>::W, Neg<DT>::W, Neg<DT>::W);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_a(sb + 8u * (ns + rp.st));   // the stage now lives in registers
+    if (++rp.st == ns) { rp.st = 0; rp.ph ^= 1u; }
+    uint32_t hb[CPT];
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) hb[j] = 0u;
+    if (p.pen) {
+        const uint32_t bm = sb + (uint32_t)P.off_bitmap;
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+            const int ch = tid + j * NCT;
+            if (ch < nch) {
+                const int c0 = tcol0 + ch * VEC;
+                const int w = c0 >> 5, b = c0 & 31;
+                const uint32_t lo = lds_u32(bm + 4u * (uint32_t)w);
+                const uint32_t hi = (b + VEC > 32 && w + 1 < P.nwords) ? lds_u32(bm + 4u * (uint32_t)(w + 1)) : 0u;
+                uint32_t bits = __funnelshift_r(lo, hi, b) & ((1u << VEC) - 1u);
+                hb[j] = bits;
+                while (bits) {
+                    const int e = __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    // rank of the column among the row's history columns
+                    const uint32_t c = (uint32_t)(c0 + e), cw = c >> 5;
+                    uint32_t rk = lds_u16(sb + (uint32_t)P.off_prefix + 2u * (cw >> 1)) +
+                                  __popc(lds_u32(bm + 4u * cw) & ((1u << (c & 31)) - 1u));
+                    if (cw & 1u) rk += __popc(lds_u32(bm + 4u * (cw - 1u)));
+                    if (rk < U) sts_u32(sb + (uint32_t)P.off_sval + 4u * rk, __float_as_uint(elem_get<DT>(v[j], e)));
+                    elem_mask<DT>(v[j], e);
+                }
+            }
+        }
+    }
+    const float m = chunks_max<DT>(v);
+    st.tmax = fmax_nan(st.tmax, m);
+    if (p.mode == MODE_GREEDY && m > st.imax) { st.imax = m; st.itile = t; }
+    if (p.zsum) {
+        st.tmin = fminf(st.tmin, chunks_min<DT>(v));
+        if (m > st.zm) {
+            const float nn = -(m * p.c);
+            const float f = ex2_approx(nn - st.nzmc);
+            st.z0 *= f; st.z1 *= f;
+            st.zm = m; st.nzmc = nn;
+        }
+        chunks_sumexp<DT>(v, p.c, st.nzmc, st.z0, st.z1);
+    }
+    if (st.cand) {
+        if constexpr (FIRST) {
+            tau0_cold<DT>(P, tid, r, v[0], v[1], m);
+            st.xmin = __uint_as_float(lds_u32(a_ctl + O_XMIN));
+        }
+        uint32_t pick = 0;
+        if (m >= st.xmin) {
+#pragma unroll
+            for (int j = 0; j < CPT; ++j) {
+                const int ch = tid + j * NCT;
+                if (ch < nch) {
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e)
+                        if (!((hb[j] >> e) & 1u) && elem_get<DT>(v[j], e) >= st.xmin) pick |= 1u << (j * VEC + e);
+                }
+            }
+        }
+        while (pick) {
+            const int i = __ffs(pick) - 1;
+            pick &= pick - 1;
+            const int j = i / VEC, e = i % VEC;
+            uint4 vv = v[0];
+#pragma unroll
+            for (int jj = 1; jj < CPT; ++jj) if (jj == j) vv = v[jj];
+            const uint32_t key = fkey(elem_get<DT>(vv, e));
+            const uint32_t col = (uint32_t)(tcol0 + (tid + j * NCT) * VEC + e);
+            // append (no warp collectives: 32-bit shared atomics on one
+            // counter are combined by the hardware)
+            const uint32_t slot = st.win % 3u;
+            const uint32_t pos = st.base + atoms_add_u32(a_ctl + O_WCNT + 4u * slot, 1u);
+            if (pos < (uint32_t)CAND_CAP) {
+                sts_u32(sb + (uint32_t)P.off_ckey + 4u * pos, key);
+                sts_u32(sb + (uint32_t)P.off_cid + 4u * pos, col);
+            } else {
+                sts_u32(a_ctl + O_OVF + 4u * slot, 1u);
+            }
+            st.khi = max(st.khi, key);
+            st.klo = min(st.klo, key);
+        }
+        // windows end where the previous check scheduled them (appends per
+        // tile fall off as 1/t, so windows widen along the row), and at the
+        // last tile; appends are bounds checked, an overflow sends the row
+        // to the multi-pass path
+        if (t == tc.next_chk || t == g.ntiles - 1) {
+            const bool need = window_end(a_ctl, tid, st, (uint32_t)HWM, tc.rate2);
+            tc.span = t - tc.last_chk;
+            tc.last_chk = t;
+            if (need) return true;   // the caller compacts, then schedules the next window
+            tc.next_chk = t + window_span(st.base, tc.rate2, tc.span, span_max_at(t));
+        }
+    }
+    return false;
+}
+
+// Compaction after a window end (outside the streaming loop), then the next
+// window's schedule.
+__device__ __forceinline__ void compact_window(const KParams& P, const int tid, const int r, const int t, Stream& st,
+                                               TileCtx& tc) {
+    const uint32_t a_ctl = smem_base32() + (uint32_t)P.off_ctl;
+    const uint32_t n = compact_cold(P, tid, r, st.base, st.klo, st.khi);
+    st.xmin = __uint_as_float(lds_u32(a_ctl + (uint32_t)offsetof(RowCtl, xmin)));
+    st.klo = max(st.klo, fkey(st.xmin));
+    st.base = n;
+    if (n > (uint32_t)HWM) st.cand = false;
+    tc.next_chk = t + window_span(n, tc.rate2, tc.span, span_max_at(t));
+}
+
+// Tile 0 of a row (kept out of line: it calls the threshold select).
+template <int DT>
+__device__ __forceinline__ void first_tile(const KParams& P, const int tid, const int r, RingPos& rp_io, Stream& st_io,
+                                        const uint32_t U, TileCtx& tc_io) {
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    RingPos rp = rp_io;
+    Stream st = st_io;
+    TileCtx tc = tc_io;
+    if (process_tile<DT, true>(P, p, g, tid, r, 0, rp, st, U, tc)) compact_window(P, tid, r, 0, st, tc);
+    rp_io = rp;
+    st_io = st;
+    tc_io = tc;
+}
+
+// Tiles [t0, ntiles) of a row until a window end asks for a compaction.
+// Contains no call, so the loop keeps its state in registers. Returns the
+// next tile; *need tells whether a compaction is due first.
+template <int DT>
+__device__ __noinline__ int stream_row(const KParams& P, const int tid, const int r, const int t0, RingPos& rp_io,
+                                       Stream& st_io, const uint32_t U, TileCtx& tc_io, bool& need) {
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    RingPos rp = rp_io;
+    Stream st = st_io;
+    TileCtx tc = tc_io;
+    int t = t0;
+    need = false;
+    for (; t < g.ntiles; ++t) {
+        if (process_tile<DT, false>(P, p, g, tid, r, t, rp, st, U, tc)) { need = true; ++t; break; }
+    }
+    rp_io = rp;
+    st_io = st;
+    tc_io = tc;
+    return t;
+}
+
+template <int DT>
+__device__ void sample_row(const KParams& P, const int tid, const int r, RingPos& rp) {
+    using E = Elem<DT>;
+    constexpr int ESZ = E::SIZE, VEC = E::VEC;
+    const int lane = tid & 31, warp = tid >> 5;
+    const uint32_t ns = (uint32_t)P.nstage;
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<ESZ>(P, r);
+    if (tid == 0) {
+        RowCtl* ctl = carve(smem_base(), P).ctl;
+        ctl->wcnt[0] = ctl->wcnt[1] = ctl->wcnt[2] = 0u;
+        ctl->ovf[0] = ctl->ovf[1] = ctl->ovf[2] = 0;
+        ctl->hikey = 0u; ctl->lokey = 0xffffffffu; ctl->xmin = -INFINITY;
+        ctl->status = p.bad; ctl->nunique = 0u;
+    }
+    csync();
+    if (p.pen) history_prologue_cold(P, tid, r);
+    const uint32_t U = p.pen ? carve(smem_base(), P).ctl->nunique : 0u;
+    Stream st;
+    st.tmax = -INFINITY; st.imax = -INFINITY; st.itile = -1; st.tmin = INFINITY;
+    st.zm = -1e30f; st.nzmc = -(st.zm * p.c); st.z0 = 0.0f; st.z1 = 0.0f;
+    st.xmin = -INFINITY; st.cand = p.cand; st.base = 0; st.win = 0;
+    st.bestv = -INFINITY; st.bestc = 0xffffffffu;
+    st.khi = 0u; st.klo = 0xffffffffu;
+
+    {
+        const RowGeom gg = row_geom<ESZ>(P, r);
+        TileCtx tc{-1, 0, 1, 0ull};
+        if (gg.ntiles > 0) first_tile<DT>(P, tid, r, rp, st, U, tc);
+        for (int t = 1; t < gg.ntiles;) {
+            bool need;
+            t = stream_row<DT>(P, tid, r, t, rp, st, U, tc, need);
+            if (need) compact_window(P, tid, r, t - 1, st, tc);
+        }
+    }
+
+    const Smem s = carve(smem_base(), P);
     RowCtl* ctl = s.ctl;
     volatile int* abort = &ctl->abort;
+    const uint8_t* rowp = reinterpret_cast<const uint8_t*>(P.logits) + (int64_t)r * P.row_stride * ESZ;
+    // ---- ragged head/tail columns (at most 2 * (VEC - 1)), one per lane of warp 0;
+    //      processed after the interior so the candidate filter is final ----
+    if (warp == 0) {
+        const int nh = g.head, nt = P.vocab - g.tail0;
+        bool valid = lane < nh + nt;
+        const int c = lane < nh ? lane : g.tail0 + (lane - nh);
+        float x = -INFINITY;
+        if (valid) {
+            x = E::load(rowp, c);
+            if (p.pen && (hist_bits(s, P.nwords, c, 1) & 1u)) {
+                const uint32_t rk = hist_rank(s, (uint32_t)c);
+                if (rk < U) s.sval[rk] = x;   // merged after the stream
+                valid = false;
+            }
+        }
+        process_one(p, s, st, x, (uint32_t)(valid ? c : 0), valid, lane);
+    }
+
+    // ---- merge the history columns with their penalised values ----
+    if (p.pen) {
+        csync();
+        for (uint32_t i0 = 0; i0 < U; i0 += NCT) {
+            const uint32_t i = i0 + tid;
+            const bool valid = i < U;
+            float x = -INFINITY;
+            uint32_t col = 0;
+            if (valid) { col = s.scol[i]; x = penalize(p, s, i, s.sval[i]); }
+            process_one(p, s, st, x, col, valid, lane);
+        }
+    }
+    // last window: nothing is appended after it, so only the limit applies
+    if (st.cand) (void)window_check(P, r, p, s, tid, st, (uint32_t)HWM + (CAND_CAP - HWM) / 2, 1 << 20, 1);
+    // uniform snapshot of the abort flag (the producer may set it at any time)
+    if (tid == 0) ctl->snap = (*abort != 0) ? 1u : 0u;
+    csync();
+    const bool aborted = ctl->snap != 0;
+
+    finish_row_cold<DT>(P, tid, r, st.tmax, st.tmin, st.z0, st.z1, st.nzmc, st.cand, st.base, st.imax, st.itile,
+                        st.bestv, st.bestc, aborted);
+    if (row_heavy(P, r)) {
+        // the producer streamed this row with an evict-last policy: release it
+        const uintptr_t a0 = reinterpret_cast<uintptr_t>(g.interior) & ~uintptr_t(127);
+        const uintptr_t a1 = reinterpret_cast<uintptr_t>(g.interior) + (uintptr_t)g.interior_bytes;
+        for (uintptr_t a = a0 + (uintptr_t)tid * 128u; a < a1; a += (uintptr_t)NCT * 128u)
+            l2_evict_normal(reinterpret_cast<const void*>(a));
+    }
+}
+
+template <int DT>
+__device__ void consumer(const KParams& P, const int tid) {
     RingPos rp{0u, 0u};
     uint32_t k = 0;
     while (true) {
-        const uint32_t slot = k % RQ, ph = (k / RQ) & 1u;
-        if (tid == 0) {
-            const bool ok = mbar_wait(&s.rowfull[slot], ph, abort);
-            ctl->snap = ok ? (uint32_t)ctl->rowq[slot] : 0xfffffffeu;
+        int r;
+        {
+            const Smem s = carve(smem_base(), P);
+            RowCtl* ctl = s.ctl;
+            volatile int* abort = &ctl->abort;
+            const uint32_t slot = k % RQ, ph = (k / RQ) & 1u;
+            if (tid == 0) {
+                const bool ok = mbar_wait(&s.rowfull[slot], ph, abort);
+                ctl->snap = ok ? (uint32_t)ctl->rowq[slot] : 0xfffffffeu;
+            }
+            csync();
+            r = (int)ctl->snap;
+            csync();
+            if (tid == 0 && r != -2) mbar_arrive(&s.rowempty[slot]);
         }
-        csync();
-        const int r = (int)ctl->snap;
-        csync();
-        if (tid == 0 && r != -2) mbar_arrive(&s.rowempty[slot]);
         ++k;
         if (r < 0) break;
-        sample_row<DT>(P, s, tid, r, rp);
-        if (tid == 0) ctl->snap = (*abort != 0) ? 1u : 0u;
-        csync();
-        const bool aborted = ctl->snap != 0;
-        csync();
+        sample_row<DT>(P, tid, r, rp);
+        bool aborted;
+        {
+            const Smem s = carve(smem_base(), P);
+            if (tid == 0) s.ctl->snap = (s.ctl->abort != 0) ? 1u : 0u;
+            csync();
+            aborted = s.ctl->snap != 0;
+            csync();
+        }
         if (aborted) break;
     }
+    const Smem s = carve(smem_base(), P);
+    RowCtl* ctl = s.ctl;
+    volatile int* abort = &ctl->abort;
     if (tid == 0 && *abort) {
         // report the rows this CTA can no longer process: published ones, then the rest
         for (;; ++k) {
@@ -1124,17 +1715,18 @@ __device__ void consumer(const KParams& P, const Smem& s, const int tid) {
         }
         for (;;) {
             const unsigned v = atomicAdd(&P.ws->next_row, 1u);
-            if (v >= (unsigned)P.batch) break;
-            P.out_ids[v] = -1;
-            if (P.out_status) P.out_status[v] = FG_ROW_TIMEOUT;
+            if (v >= 2u * (unsigned)P.batch) break;
+            if (!row_owned(P, v)) continue;   // handed out in the other half of the queue
+            const unsigned rr = v % (unsigned)P.batch;
+            P.out_ids[rr] = -1;
+            if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT;
         }
     }
 }
 
 template <int DT>
-__global__ void __launch_bounds__(NTHREADS, 2) fg_sample_kernel(const KParams P) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    const Smem s = carve(smem_raw, P);
+__global__ void __launch_bounds__(NTHREADS, 2) fg_sample_kernel(const __grid_constant__ KParams P) {
+    const Smem s = carve(smem_base(), P);
     const int tid = threadIdx.x;
     if (tid == 0) {
         for (int i = 0; i < P.nstage; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], NCW); }
@@ -1147,7 +1739,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) fg_sample_kernel(const KParams P)
         if (tid == NCT) producer<DT>(P, s);
         return;
     }
-    consumer<DT>(P, s, tid);
+    consumer<DT>(P, tid);
     // the last CTA to finish leaves the workspace zeroed for the next launch
     csync();
     if (tid == 0) {

@@ -70,6 +70,7 @@ struct KParams {
     int32_t nstage;
     int32_t nwords;          // history bitmap words
     int32_t hu_cap;          // unique-history capacity (0: no penalties possible)
+    int32_t off_ctl;         // RowCtl
     int32_t off_bins, off_cnts, off_ckey, off_cid;
     int32_t off_bitmap, off_prefix, off_counts, off_sval, off_scol, off_ring;
     int32_t pen_possible;
@@ -129,6 +130,28 @@ __host__ __device__ inline int head_bytes(int nstage) {
     o = align_up_i(o, 16) + (8 + 4 + 4 + 8) * NCW;
     return align_up_i(o, 128);
 }
+
+// The kernel's dynamic shared memory (every unsized extern __shared__ array
+// starts at the same address).
+extern __shared__ __align__(128) uint8_t fg_smem[];
+// Its base, passed through an empty asm so the optimizer cannot hoist the
+// pointers derived from it out of a loop: rebuilding the layout where it is
+// used (a few integer adds from the grid-constant offsets) is cheaper than
+// holding twenty 64-bit pointers live across the streaming loop.
+__device__ __forceinline__ uint8_t* smem_base() {
+    uint8_t* b = fg_smem;
+    asm volatile("" : "+l"(b));
+    return b;
+}
+
+// 32-bit shared-window address of the dynamic shared memory, opaque in the
+// same way (one instruction where it is used).
+__device__ __forceinline__ uint32_t smem_base32() {
+    uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(fg_smem));
+    asm volatile("" : "+r"(b));
+    return b;
+}
+__host__ __device__ inline int ctl_offset(int nstage) { return align_up_i(8 * (2 * nstage + 2 * RQ), 16); }
 
 __device__ __forceinline__ Smem carve(uint8_t* base, const KParams& P) {
     Smem s;
@@ -241,6 +264,25 @@ __device__ __forceinline__ RowParams row_params(const KParams& P, int r) {
     return p;
 }
 
+// Row queue: entries [0, B) hand out the rows that may need passes over the
+// row after the stream (sampling rows whose top-k is off or above the
+// candidate limit), entries [B, 2B) the other rows, so the long rows start
+// first. Each entry belongs to the half that owns its row; a producer claims
+// ROW_CLAIM entries per atomic.
+constexpr int ROW_CLAIM = 4;
+__device__ __forceinline__ bool row_heavy(const KParams& P, int r) {
+    const float T = __ldg(P.temperature + r);
+    const bool g = P.greedy ? (__ldg(P.greedy + r) != 0) : false;
+    const int tk = __ldg(P.top_k + r);
+    if (g || T == 0.0f) return false;
+    return tk <= 0 || tk > K_FAST_MAX;
+}
+__device__ __forceinline__ bool row_owned(const KParams& P, unsigned v) {
+    const unsigned B = (unsigned)P.batch;
+    if (v >= 2u * B) return false;
+    return (v < B) == row_heavy(P, (int)(v % B));
+}
+
 __device__ __forceinline__ float ydiv(const RowParams& p, float x) {
     return p.temp_on ? div_rn(x, p.T, p.rT) : x;
 }
@@ -262,6 +304,43 @@ __device__ float xmin_for(const RowParams& p, float tau) {
         if (ydiv(p, funkey(mid)) >= yt) hi = mid; else lo = mid + 1;
     }
     return funkey(hi);
+}
+
+// Smallest x with fkey(y(x)) >= yk (y is monotone in x). Starts from
+// yk's value times T and walks a few keys; bisects over the key space if the
+// walk is long. Identical in every thread (no barrier).
+constexpr uint32_t KEY_POS_INF = 0xff800000u;
+__device__ float x_lower(const RowParams& p, uint32_t yk) {
+    if (yk <= KEY_NEG_INF) return -INFINITY;
+    if (!p.temp_on) return funkey(yk);
+    auto pred = [&](uint32_t k) { return fkey(ydiv(p, funkey(k))) >= yk; };
+    if (yk > KEY_POS_INF || !pred(KEY_POS_INF)) return NAN;   // no such x
+    const float g = funkey(yk) * p.T;
+    uint32_t k = (g == g) ? fkey(g) : KEY_POS_INF;
+    if (k < KEY_NEG_INF) k = KEY_NEG_INF;
+    if (k > KEY_POS_INF) k = KEY_POS_INF;
+    for (int steps = 0; steps < 8; ++steps) {
+        if (pred(k)) {
+            if (k <= KEY_NEG_INF || !pred(k - 1)) return funkey(k);
+            --k;
+        } else {
+            ++k;   // k < KEY_POS_INF, where pred holds
+        }
+    }
+    uint32_t lo = KEY_NEG_INF, hi = KEY_POS_INF;
+    while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo) / 2;
+        if (pred(mid)) hi = mid; else lo = mid + 1;
+    }
+    return funkey(lo);
+}
+// Largest x with fkey(y(x)) <= yk.
+__device__ float x_upper(const RowParams& p, uint32_t yk) {
+    if (yk >= KEY_POS_INF) return INFINITY;
+    const float xn = x_lower(p, yk + 1u);
+    if (!(xn == xn)) return INFINITY;
+    const uint32_t kn = fkey(xn);
+    return kn <= KEY_NEG_INF ? -INFINITY : funkey(kn - 1u);
 }
 
 // ---------------------------------------------------------------------------
