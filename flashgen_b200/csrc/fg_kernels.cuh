@@ -181,20 +181,35 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
     }
     if (bad) atomicOr(&s.ctl->status, FG_ROW_BAD_HISTORY);
     csync();
-    // thread t owns the word pairs [q0, q1): prefix counts and the scol entries
-    const int ppt = (npair + NCT - 1) / NCT;
-    const int q0 = tid * ppt, q1 = min(npair, q0 + ppt);
-    uint32_t local = 0;
-    for (int q = q0; q < q1; ++q) {
-        local += __popc(s.bitmap[2 * q]);
-        if (2 * q + 1 < nw) local += __popc(s.bitmap[2 * q + 1]);
+    // popcount prefix per 64-column pair of words, in pair order: warp w owns
+    // pairs [w * ppw, (w + 1) * ppw), its lanes take 32 consecutive pairs at a
+    // time (two-way bank conflicts at most)
+    const int ppw = (npair + NCW - 1) / NCW;
+    const int wq0 = (tid >> 5) * ppw, wq1 = min(npair, wq0 + ppw);
+    auto pair_pop = [&](int q) -> uint32_t {
+        if (q >= wq1) return 0u;
+        return __popc(s.bitmap[2 * q]) + (2 * q + 1 < nw ? __popc(s.bitmap[2 * q + 1]) : 0);
+    };
+    uint32_t wsum = 0;
+    for (int q0 = wq0; q0 < wq1; q0 += 32) wsum += pair_pop(q0 + lane);
+    wsum = __reduce_add_sync(0xffffffffu, wsum);
+    if (lane == 0) s.red32[tid >> 5] = wsum;
+    csync();
+    uint32_t run = 0, total = 0;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) {
+        const uint32_t c = s.red32[i];
+        if (i < (tid >> 5)) run += c;
+        total += c;
     }
-    uint32_t total;
-    uint32_t run = cons_excl_scan_u32(local, total, s, tid);
+    csync();
     const uint32_t cap = (uint32_t)P.hu_cap;
-    for (int q = q0; q < q1; ++q) {
-        s.prefix[q] = (uint16_t)run;
-        run += __popc(s.bitmap[2 * q]) + (2 * q + 1 < nw ? __popc(s.bitmap[2 * q + 1]) : 0);
+    for (int q0 = wq0; q0 < wq1; q0 += 32) {
+        const int q = q0 + lane;
+        const uint32_t c = pair_pop(q);
+        const uint32_t incl = warp_incl_scan_u32(c, lane);
+        if (q < wq1) s.prefix[q] = (uint16_t)(run + incl - c);
+        run += __shfl_sync(0xffffffffu, incl, 31);
     }
     csync();
     // ascending list of distinct columns: words strided over the threads
@@ -308,47 +323,90 @@ __device__ __forceinline__ void process_one(const RowParams& p, const Smem& s, S
 // Compaction: exact K-th largest candidate key -> xmin; drop keys below it
 // (stable, in place). Returns the new candidate count.
 // ---------------------------------------------------------------------------
-__device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t n, Stream& st) {
+// Order-preserving 16-bit keys of unpenalised 16-bit logits (key16 order ==
+// key order), and back. bf16: the top half of the 32-bit key (its low half is
+// 0x0000 for positive values, 0xffff for negative ones). fp16: the key of the
+// half's own bit pattern.
+__device__ __forceinline__ uint32_t key16_of(uint32_t k, int dt16) {
+    if (dt16 == FG_DTYPE_BF16) return k >> 16;
+    const uint32_t h = __half_as_ushort(__float2half_rn(funkey(k)));
+    return (h & 0x8000u) ? (~h & 0xffffu) : (h | 0x8000u);
+}
+__device__ __forceinline__ uint32_t key_from16(uint32_t k16, int dt16) {
+    if (dt16 == FG_DTYPE_BF16) return (k16 << 16) | ((k16 & 0x8000u) ? 0u : 0xffffu);
+    const uint32_t h = (k16 & 0x8000u) ? (k16 & 0x7fffu) : (~k16 & 0xffffu);
+    return fkey(__half2float(__ushort_as_half((unsigned short)h)));
+}
+
+// Block min and max of a u32 in one barrier round.
+__device__ __forceinline__ void cons_minmax_u32(uint32_t& mn, uint32_t& mx, const Smem& s, int tid) {
+    mn = __reduce_min_sync(0xffffffffu, mn);
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    if ((tid & 31) == 0) { s.red32[tid >> 5] = mn; reinterpret_cast<uint32_t*>(s.redf)[tid >> 5] = mx; }
+    csync();
+    uint32_t a = s.red32[0], b = reinterpret_cast<const uint32_t*>(s.redf)[0];
+#pragma unroll
+    for (int w = 1; w < NCW; ++w) { a = min(a, s.red32[w]); b = max(b, reinterpret_cast<const uint32_t*>(s.redf)[w]); }
+    csync();
+    mn = a; mx = b;
+}
+
+// ---------------------------------------------------------------------------
+// Compaction: exact K-th largest candidate key -> xmin; drop keys below it.
+// dt16 (FG_DTYPE_BF16 / FG_DTYPE_F16, else 0): every candidate is an
+// unpenalised 16-bit logit, so the select runs on 16-bit keys (two 8-bit
+// passes). The kept entries are
+// rewritten in any order (nothing downstream depends on it): every thread
+// holds its CAND_CAP / NCT entries in registers, then writes the kept ones at
+// positions from one atomic per warp. Returns the new candidate count.
+// ---------------------------------------------------------------------------
+__device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t n, Stream& st, int dt16) {
+    static_assert(CAND_CAP % NCT == 0, "entries per thread");
+    constexpr int PER = CAND_CAP / NCT;
     RowCtl* ctl = s.ctl;
     if (n <= (uint32_t)p.K) return n;
-    const uint32_t lo = cons_min_u32(st.klo, s, tid), hi = cons_max_u32(st.khi, s, tid);
+    uint32_t lo = st.klo, hi = st.khi;
+    cons_minmax_u32(lo, hi, s, tid);
     if (lo > hi) return n;
+    if (tid == 0) ctl->ncol = 0u;
+    auto kx = [&](uint32_t k) { return dt16 ? key16_of(k, dt16) : k; };
+    const uint32_t lo_x = kx(lo), hi_x = kx(hi);
     const SelOut so = block_select<true, true>(
         [&](auto&& f) {
             for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
                 const uint32_t i = i0 + tid;
-                f(i < n, i < n ? s.ckey[i] : 0u, 1ull);
+                f(i < n, i < n ? kx(s.ckey[i]) : 0u, 1ull);
             }
         },
-        (uint64_t)(p.K - 1), lo, varying_bits(lo, hi), s, tid);
+        (uint64_t)(p.K - 1), lo_x, varying_bits(lo_x, hi_x), s, tid);
     if (!so.ok) return n;
     if (tid == 0) {
-        const float xm = xmin_for(p, funkey(so.key));
+        const float xm = xmin_for(p, funkey(dt16 ? key_from16(so.key, dt16) : so.key));
         if (xm > ctl->xmin) ctl->xmin = xm;
     }
-    csync();
+    uint32_t kk[PER], ii[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const uint32_t idx = (uint32_t)(j * NCT + tid);
+        kk[j] = idx < n ? s.ckey[idx] : 0u;
+        ii[j] = idx < n ? s.cid[idx] : 0u;
+    }
+    csync();   // every entry is in registers and xmin is published
     const uint32_t kmin = fkey(ctl->xmin);
     st.klo = max(st.klo, kmin);
-    uint32_t out = 0;
-    for (uint32_t base = 0; base < n; base += NCT * 8) {
-        uint32_t kk[8], ii[8], keep = 0, cnt = 0;
-        const uint32_t i0 = base + tid * 8;
+    uint32_t cnt = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint32_t idx = i0 + j;
-            kk[j] = idx < n ? s.ckey[idx] : 0u;
-            ii[j] = idx < n ? s.cid[idx] : 0u;
-            if (idx < n && kk[j] >= kmin) { keep |= 1u << j; ++cnt; }
-        }
-        uint32_t total;
-        uint32_t pos = out + cons_excl_scan_u32(cnt, total, s, tid);
+    for (int j = 0; j < PER; ++j) cnt += ((uint32_t)(j * NCT + tid) < n && kk[j] >= kmin) ? 1u : 0u;
+    const int lane = tid & 31;
+    const uint32_t incl = warp_incl_scan_u32(cnt, lane);
+    uint32_t base = 0;
+    if (lane == 31) base = atomicAdd(&ctl->ncol, incl);
+    base = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (keep >> j & 1u) { s.ckey[pos] = kk[j]; s.cid[pos] = ii[j]; ++pos; }
-        out += total;
-        csync();
-    }
-    return out;
+    for (int j = 0; j < PER; ++j)
+        if ((uint32_t)(j * NCT + tid) < n && kk[j] >= kmin) { s.ckey[base] = kk[j]; s.cid[base] = ii[j]; ++base; }
+    csync();
+    return ctl->ncol;
 }
 
 // End of a candidate window, without any call (the streaming loop must not
@@ -388,13 +446,13 @@ __device__ __forceinline__ int span_max_at(int t) { return t < 4 ? 1 : (t < 16 ?
 // overflow it at twice this window's append rate. Returns the number of tiles
 // (a power of two <= span_max) the next window may cover at that rate.
 __device__ __forceinline__ uint32_t compact_cold(const KParams& P, int tid, int r, uint32_t n, uint32_t klo,
-                                              uint32_t khi) {
+                                              uint32_t khi, int dt16) {
     const Smem s = carve(smem_base(), P);
     const RowParams p = row_params(P, r);
     Stream st;
     st.klo = klo;
     st.khi = khi;
-    return compact(p, s, tid, n, st);
+    return compact(p, s, tid, n, st, dt16);
 }
 
 __device__ __forceinline__ int window_check(const KParams& P, int r, const RowParams& p, const Smem& s, int tid,
@@ -416,7 +474,7 @@ __device__ __forceinline__ int window_check(const KParams& P, int r, const RowPa
                        (uint64_t)CAND_CAP;
             };
             if (n > limit || !fits(n, 1)) {
-                n = compact_cold(P, tid, r, n, st.klo, st.khi);
+                n = compact_cold(P, tid, r, n, st.klo, st.khi, 0);
                 st.klo = max(st.klo, fkey(s.ctl->xmin));
                 if (n > limit) st.cand = false;
             }
@@ -798,7 +856,7 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
     const double sc = (double)scale;
     const double T = (double)target;
     uint64_t above = 0;
-    bool beyond = false;
+    bool beyond = false, single = false;
     for (int d = 0;; ++d) {
         const float span = wu - wl;
         float inv = span > 0.0f ? (float)NW / span : 0.0f;
@@ -808,11 +866,21 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
         csync();
         uint64_t acc = 0;
         const float a0 = wl, a1 = wu, bi = inv;
-        for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
-            if (!valid || !(x >= xlo && x <= xhi)) return;
-            if (x > a1) acc += q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
-            else if (x >= a0) atomicAdd(&cnt[wbin(x, a0, bi)], 1u);
-        });
+        if (d == 0) {
+            // nothing lies above level 0's range: counts only
+            for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+                if (valid && x >= a0 && x <= xhi && x >= xlo) atomicAdd(&cnt[wbin(x, a0, bi)], 1u);
+            });
+        } else {
+            // branch-free per element: the mass is computed for every element
+            // and added under a predicate, so a warp does not run both paths
+            for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+                const bool inr = valid && x >= xlo && x <= xhi;
+                const uint64_t q = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+                acc += (inr && x > a1) ? q : 0ull;
+                if (inr && x <= a1 && x >= a0) atomicAdd(&cnt[wbin(x, a0, bi)], 1u);
+            });
+        }
         csync();
         if (d > 0) above = cons_sum_u64(acc, s, tid);
         const WWin win = wscan(s, cnt, wl, wu, inv, sx, p, My, sc, (double)above, T, tid);
@@ -830,10 +898,38 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
         wl = nl;
         wu = nu;
         if (win.count <= fit) break;
+        // a window of one value (a run of ties longer than the free buffer)
+        // cannot be split further, and need not be collected
+        if (fkey(ydiv(p, wl)) == fkey(ydiv(p, wu))) { single = true; break; }
         if (d + 1 >= WDEPTH || !progress) {
             W.fallback = true;
             return W;
         }
+    }
+    if (single) {
+        // exact mass above the run and its length; every element of the run
+        // has the same y, hence the same mass
+        const float a0 = wl, a1 = wu;
+        uint64_t accA = 0, cnt = 0;
+        for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+            const bool inr = valid && x >= xlo && x <= xhi;
+            const uint64_t q = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+            accA += (inr && x > a1) ? q : 0ull;
+            cnt += (inr && x <= a1 && x >= a0) ? 1u : 0u;
+        });
+        const uint64_t A = cons_sum_u64(accA, s, tid);
+        const uint64_t n_at = cons_sum_u64(cnt, s, tid);
+        const uint32_t key = fkey(ydiv(p, wl));
+        const uint64_t q = q_of(efast(funkey(key), My), scale);
+        if (target < A) { W.fallback = true; return W; }   // bracket violated: take the exact path
+        if (n_at == 0 || target >= A + n_at * q) {
+            L.total = region_mass<DT>(P, s, p, r, g, tid, rlo, rhi, My, scale);
+            if (target < L.total) W.fallback = true;
+            return W;
+        }
+        L.ok = true; L.in_buffer = false; L.key = key; L.before = A; L.at = n_at * q; L.n_at = (uint32_t)n_at;
+        L.total = A + n_at * q;
+        return W;
     }
     if (beyond) {
         // the target lies at or past the region's total mass
@@ -850,7 +946,8 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
     for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
         const bool inr = valid && x >= xlo && x <= xhi;
         const bool in = inr && x >= a0 && x <= a1;
-        if (inr && x > a1) accA += q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+        const uint64_t qa = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+        accA += (inr && x > a1) ? qa : 0ull;
         const uint32_t bal = __ballot_sync(0xffffffffu, in);
         if (bal) {
             const int lead = __ffs(bal) - 1;
@@ -1340,28 +1437,32 @@ __device__ __forceinline__ void tau0_cold(const KParams& P, int tid, int r, uint
     if (K <= NCT / 2) lo_v = m;
     else if (K <= NCT) { for (int j = 0; j < CPT; ++j) lo_v = fminf(lo_v, cm[j]); }
     else lo_v = chunks_min<DT>(v);
-    const uint32_t klo = cons_min_u32((lo_v == lo_v && lo_v > -INFINITY) ? fkey(lo_v) : 0xffffffffu, s, tid);
-    const uint32_t khi = cons_max_u32((m == m && m > -INFINITY) ? fkey(m) : 0u, s, tid);
+    // keys of the tile's raw values: 16-bit keys for the 16-bit dtypes
+    auto kx = [&](float x) { return DT == FG_DTYPE_F32 ? fkey(x) : key16_of(fkey(x), DT); };
+    uint32_t klo = (lo_v == lo_v && lo_v > -INFINITY) ? kx(lo_v) : 0xffffffffu;
+    uint32_t khi = (m == m && m > -INFINITY) ? kx(m) : 0u;
+    cons_minmax_u32(klo, khi, s, tid);
+    const int kbits = DT == FG_DTYPE_F32 ? 32 : 16;
     const SelOut so = block_select<true, true>(
         [&](auto&& f) {
             if (K <= NCT / 2) {
-                f(m == m && m > -INFINITY, fkey(m), 1ull);
+                f(m == m && m > -INFINITY, m == m ? kx(m) : 0u, 1ull);
             } else if (K <= NCT) {
 #pragma unroll
-                for (int j = 0; j < CPT; ++j) f(cm[j] == cm[j] && cm[j] > -INFINITY, fkey(cm[j]), 1ull);
+                for (int j = 0; j < CPT; ++j) f(cm[j] == cm[j] && cm[j] > -INFINITY, cm[j] == cm[j] ? kx(cm[j]) : 0u, 1ull);
             } else {
 #pragma unroll
                 for (int j = 0; j < CPT; ++j)
 #pragma unroll
                     for (int e = 0; e < VEC; ++e) {
                         const float x = elem_get<DT>(v[j], e);
-                        f(x == x && x > -INFINITY, fkey(x), 1ull);
+                        f(x == x && x > -INFINITY, x == x ? kx(x) : 0u, 1ull);
                     }
             }
         },
-        (uint64_t)(K - 1), klo <= khi ? klo : 0u, klo <= khi ? varying_bits(klo, khi) : 32, s, tid);
+        (uint64_t)(K - 1), klo <= khi ? klo : 0u, klo <= khi ? varying_bits(klo, khi) : kbits, s, tid);
     if (so.ok && tid == 0) {
-        const float xm = xmin_for(p, funkey(so.key));
+        const float xm = xmin_for(p, funkey(DT == FG_DTYPE_F32 ? so.key : key_from16(so.key, DT)));
         if (xm > ctl->xmin) ctl->xmin = xm;
     }
     csync();
@@ -1531,9 +1632,9 @@ __device__ __forceinline__ bool process_tile(const KParams& P, const RowParams& 
 // Compaction after a window end (outside the streaming loop), then the next
 // window's schedule.
 __device__ __forceinline__ void compact_window(const KParams& P, const int tid, const int r, const int t, Stream& st,
-                                               TileCtx& tc) {
+                                               TileCtx& tc, int dt16) {
     const uint32_t a_ctl = smem_base32() + (uint32_t)P.off_ctl;
-    const uint32_t n = compact_cold(P, tid, r, st.base, st.klo, st.khi);
+    const uint32_t n = compact_cold(P, tid, r, st.base, st.klo, st.khi, dt16);
     st.xmin = __uint_as_float(lds_u32(a_ctl + (uint32_t)offsetof(RowCtl, xmin)));
     st.klo = max(st.klo, fkey(st.xmin));
     st.base = n;
@@ -1550,7 +1651,7 @@ __device__ __forceinline__ void first_tile(const KParams& P, const int tid, cons
     RingPos rp = rp_io;
     Stream st = st_io;
     TileCtx tc = tc_io;
-    if (process_tile<DT, true>(P, p, g, tid, r, 0, rp, st, U, tc)) compact_window(P, tid, r, 0, st, tc);
+    if (process_tile<DT, true>(P, p, g, tid, r, 0, rp, st, U, tc)) compact_window(P, tid, r, 0, st, tc, DT == FG_DTYPE_F32 ? 0 : DT);
     rp_io = rp;
     st_io = st;
     tc_io = tc;
@@ -1610,7 +1711,7 @@ __device__ void sample_row(const KParams& P, const int tid, const int r, RingPos
         for (int t = 1; t < gg.ntiles;) {
             bool need;
             t = stream_row<DT>(P, tid, r, t, rp, st, U, tc, need);
-            if (need) compact_window(P, tid, r, t - 1, st, tc);
+            if (need) compact_window(P, tid, r, t - 1, st, tc, DT == FG_DTYPE_F32 ? 0 : DT);
         }
     }
 
