@@ -11,7 +11,7 @@ import threading
 
 from . import build as _build
 
-FG_OK, FG_EINVAL, FG_ELAUNCH, FG_ENOTSUP, FG_EDEVICE = 0, 1, 2, 3, 4
+FG_OK, FG_EINVAL, FG_ELAUNCH, FG_ENOTSUP, FG_EDEVICE, FG_ESCRATCH = 0, 1, 2, 3, 4, 5
 FG_DTYPE_F32, FG_DTYPE_F16, FG_DTYPE_BF16 = 0, 1, 2
 
 FG_ROW_NAN = 0x0001
@@ -25,7 +25,8 @@ FG_ROW_ERROR_MASK = 0x00FF
 FG_ROW_GENERAL_PATH = 0x0100
 FG_ROW_GREEDY = 0x0200
 
-EXPORTED_SYMBOLS = ("fg_sample", "fg_apply_repetition_penalty", "fg_argmax", "fg_strerror", "fg_version")
+EXPORTED_SYMBOLS = ("fg_sample", "fg_sample_noalloc", "fg_apply_repetition_penalty", "fg_argmax", "fg_strerror",
+                    "fg_version")
 
 
 class FgSampleArgs(ctypes.Structure):
@@ -84,6 +85,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib = ctypes.CDLL(path)
         lib.fg_sample.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p]
         lib.fg_sample.restype = ctypes.c_int
+        lib.fg_sample_noalloc.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p]
+        lib.fg_sample_noalloc.restype = ctypes.c_int
         lib.fg_apply_repetition_penalty.argtypes = [
             ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]

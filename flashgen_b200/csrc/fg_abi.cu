@@ -82,6 +82,7 @@ const char* fg_strerror(int code) {
         case FG_ELAUNCH: return "kernel launch failed";
         case FG_ENOTSUP: return "shape beyond on-chip limits of this build";
         case FG_EDEVICE: return "device query or configuration failed";
+        case FG_ESCRATCH: return "request exceeds the fixed scratch of fg_sample_noalloc";
         default: return "unknown error";
     }
 }
@@ -169,6 +170,48 @@ int fg_sample(const FgSampleArgs* a, void* stream) {
         case FG_DTYPE_F16: return launch_sample<FG_DTYPE_F16>(P, smem, grid, st, d);
         default: return launch_sample<FG_DTYPE_BF16>(P, smem, grid, st, d);
     }
+}
+
+// ---------------------------------------------------------------------------
+// fg_sample without a caller workspace. Its callers cannot hand the library
+// device memory: a C++ engine whose decode loop must not allocate (an
+// allocation there can synchronise the device or fail mid-step), and a host
+// that binds the library through a plain FFI with no device allocator of its
+// own. The row-queue counters live in a file-scope __device__ array instead
+// (one per device context). Its address is looked up once per device, on the
+// first call with that device current, which also clears it on the call's
+// stream; make that first call before any stream capture. Every launch
+// leaves the counters zero again. Calls that overlap on the GPU (different
+// streams) share the counters and race: serialise them.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchBytes = 256;
+constexpr int32_t kNoAllocMaxBatch = 1 << 30;   // the queue counter runs to about 2 * batch in 32 bits
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+void* g_noalloc_ptr[kMaxDevices] = {};
+static_assert(FG_SAMPLE_WORKSPACE_BYTES <= kNoAllocScratchBytes, "static scratch smaller than the workspace");
+}  // namespace
+
+int fg_sample_noalloc(const FgSampleArgs* a, void* stream) {
+    if (a == nullptr || a->workspace != nullptr) return FG_EINVAL;
+    if (a->batch > kNoAllocMaxBatch) return FG_ESCRATCH;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FG_EDEVICE;
+    void* ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (g_noalloc_ptr[dev] == nullptr) {
+            void* p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return FG_EDEVICE;
+            if (cudaMemsetAsync(p, 0, kNoAllocScratchBytes, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+                return FG_EDEVICE;
+            g_noalloc_ptr[dev] = p;
+        }
+        ws = g_noalloc_ptr[dev];
+    }
+    FgSampleArgs b = *a;
+    b.workspace = ws;
+    return fg_sample(&b, stream);
 }
 
 int fg_argmax(const void* logits, int32_t dtype, int32_t batch, int32_t vocab, int64_t row_stride,

@@ -41,6 +41,7 @@ extern "C" {
 #define FG_ELAUNCH     2  /* the CUDA launch failed (cudaGetLastError)            */
 #define FG_ENOTSUP     3  /* shape valid but beyond this build's on-chip limits   */
 #define FG_EDEVICE     4  /* querying or configuring the current device failed    */
+#define FG_ESCRATCH    5  /* request exceeds fg_sample_noalloc's fixed scratch    */
 
 /* ---- logits element types ------------------------------------------------- */
 #define FG_DTYPE_F32   0
@@ -139,6 +140,18 @@ typedef struct FgSampleArgs {
  * `stream` is a cudaStream_t (NULL = legacy default stream).
  */
 int fg_sample(const FgSampleArgs* args, void* stream);
+
+/*
+ * fg_sample without a caller workspace: args->workspace must be NULL, and the
+ * row-queue counters live in a 256-byte static device array (one per device).
+ * No reference counterpart: FlashGen has no native sampler entry point; this
+ * one serves callers that cannot allocate device memory on the decode path
+ * (an engine loop that must not allocate, a plain-FFI host with no device
+ * allocator). The first call on a device looks up and clears the array on
+ * `stream` — make it before any stream capture. Calls that overlap on the GPU
+ * race on the array: serialise them. batch above 2^30 returns FG_ESCRATCH.
+ */
+int fg_sample_noalloc(const FgSampleArgs* args, void* stream);
 
 /*
  * In-place repetition penalty on a [batch, vocab] logits buffer: for every

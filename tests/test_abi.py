@@ -75,3 +75,15 @@ def test_validation_without_gpu():
     assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # ids without offsets
     assert lib.fg_argmax(None, 0, 1, 8, 8, None, None) == _lib.FG_EINVAL
     assert lib.fg_strerror(_lib.FG_ENOTSUP).decode().startswith("shape")
+
+
+def test_noalloc_validation_without_gpu():
+    lib = _lib.load()
+    assert lib.fg_sample_noalloc(None, None) == _lib.FG_EINVAL
+    a = _lib.FgSampleArgs()
+    a.workspace = 256
+    assert lib.fg_sample_noalloc(ctypes.byref(a), None) == _lib.FG_EINVAL   # takes no workspace
+    a.workspace = None
+    a.batch = (1 << 30) + 1
+    assert lib.fg_sample_noalloc(ctypes.byref(a), None) == _lib.FG_ESCRATCH
+    assert "scratch" in lib.fg_strerror(_lib.FG_ESCRATCH).decode()
