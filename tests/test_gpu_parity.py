@@ -214,3 +214,75 @@ def test_unaligned_rows_large_nucleus(cuda_device, seed):
     p.top_p[:] = [0.9, 0.97, 0.5, 0.999, 0.8, 0.95]
     stats, ids, status = _check(_workload(logits, p, seed=seed))
     assert (status & _lib.FG_ROW_GENERAL_PATH).any()
+
+
+def _penalised_y(w, dev):
+    """Penalised, temperature-scaled logits of a workload, with torch ops on the
+    GPU (the oracle's chain: repetition on unique ids, then presence/frequency,
+    then x / T), for checks at full size."""
+    B, V = w.batch, w.vocab
+    x = w.logits.to(dev).float()
+    p = w.params
+    counts = torch.zeros(B, V, dtype=torch.float32, device=dev)
+    rows = torch.repeat_interleave(torch.arange(B, device=dev),
+                                   torch.from_numpy(np.diff(w.hist_offsets)).to(dev))
+    counts.index_put_((rows, torch.from_numpy(w.hist_ids).long().to(dev)),
+                      torch.ones(rows.numel(), device=dev), accumulate=True)
+    rep = torch.from_numpy(p.repetition_penalty).to(dev)[:, None]
+    pres = torch.from_numpy(p.presence_penalty).to(dev)[:, None]
+    freq = torch.from_numpy(p.frequency_penalty).to(dev)[:, None]
+    seen = counts > 0
+    xr = torch.where(x > 0, x / rep, x * rep)
+    x = torch.where(seen, xr, x)
+    x = torch.where(seen, (x - freq * counts) - pres, x)
+    T = torch.from_numpy(p.temperature).to(dev)[:, None]
+    return torch.where(T > 0, x / torch.where(T > 0, T, torch.ones_like(T)), x)
+
+
+def test_full_size_properties(cuda_device):
+    """Configuration 3 at its full size (B=1024, V=128256 bf16): size-independent
+    properties on every row, and the oracle on a prefix of rows."""
+    dev = cuda_device
+    w = make_workload(3, seed=11)
+    ids, status, _ = run_kernel(w)
+    assert not (status & _lib.FG_ROW_ERROR_MASK).any()
+    ids2, status2, _ = run_kernel(w)
+    np.testing.assert_array_equal(ids, ids2)          # deterministic
+    np.testing.assert_array_equal(status, status2)
+    y = _penalised_y(w, dev)
+    p = w.params
+    greedy = (p.temperature == 0) | p.greedy
+    # greedy rows: first index of the maximum of the penalised logits
+    g_rows = np.nonzero(greedy)[0]
+    if len(g_rows):
+        want = torch.argmax(y[torch.from_numpy(g_rows).to(dev)], dim=1).cpu().numpy()
+        np.testing.assert_array_equal(ids[g_rows], want)
+    # top-k rows: the drawn token is at or above the row's k-th largest value
+    k_rows = np.nonzero(~greedy & (p.top_k > 0))[0]
+    for k in np.unique(p.top_k[k_rows]):
+        rr = k_rows[p.top_k[k_rows] == k]
+        yr = y[torch.from_numpy(rr).to(dev)]
+        kth = torch.topk(yr, int(k), dim=1).values[:, -1]
+        got = yr.gather(1, torch.from_numpy(ids[rr]).long().to(dev)[:, None])[:, 0]
+        assert bool((got >= kth).all()), rr[(got < kth).cpu().numpy()][:8]
+    # every drawn id is a valid column
+    assert ((ids >= 0) & (ids < w.vocab)).all()
+    # a prefix of the full batch against the oracle
+    n = 16
+    res = O.sample_rows(w.logits[:n], p.slice(0, n), w.histories()[:n], w.uniforms[:n])
+    ok = (ids[:n] == res.ids) | res.near_u | res.near_p
+    assert ok.all(), (np.nonzero(~ok)[0], ids[:n][~ok], res.ids[~ok])
+
+
+def test_full_size_all_greedy_equals_argmax(cuda_device):
+    dev = cuda_device
+    w = make_workload(3, seed=12)
+    w.params.greedy[:] = True
+    w.hist_offsets[:] = 0          # no history: greedy is the plain argmax
+    w.hist_ids = np.zeros(0, np.int32)
+    ids, status, _ = run_kernel(w, hist=False)
+    assert not (status & _lib.FG_ROW_ERROR_MASK).any()
+    want = torch.argmax(w.logits.to(dev), dim=1).cpu().numpy()
+    np.testing.assert_array_equal(ids, want)
+    from flashgen_b200.sampling.sampler import Sampler
+    np.testing.assert_array_equal(Sampler.argmax(w.logits.to(dev)).cpu().numpy(), want)
