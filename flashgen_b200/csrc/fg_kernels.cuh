@@ -111,6 +111,45 @@ __device__ __forceinline__ float chunks_min(const uint4 (&v)[CPT]) {
     return r;
 }
 
+// Bit e set when element e of the chunk is >= xmin. For the 16-bit types
+// x2 holds xmin rounded up to the type, in both halves: for a 16-bit x,
+// x >= xmin exactly when x >= that value, so one packed compare tests two
+// elements. NaN compares false.
+template <int DT>
+__device__ __forceinline__ uint32_t chunk_ge(const uint4& v, float xmin, uint32_t x2) {
+    if constexpr (DT == FG_DTYPE_F32) {
+        return (uint32_t)(__uint_as_float(v.x) >= xmin) | ((uint32_t)(__uint_as_float(v.y) >= xmin) << 1) |
+               ((uint32_t)(__uint_as_float(v.z) >= xmin) << 2) | ((uint32_t)(__uint_as_float(v.w) >= xmin) << 3);
+    } else {
+        uint32_t m[4];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if constexpr (DT == FG_DTYPE_BF16)
+                m[q] = __hge2_mask(*reinterpret_cast<const __nv_bfloat162*>(&w[q]),
+                                   *reinterpret_cast<const __nv_bfloat162*>(&x2));
+            else
+                m[q] = __hge2_mask(*reinterpret_cast<const __half2*>(&w[q]), *reinterpret_cast<const __half2*>(&x2));
+        }
+        uint32_t b = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) b |= ((m[q] & 1u) | ((m[q] >> 15) & 2u)) << (2 * q);
+        return b;
+    }
+}
+template <int DT>
+__device__ __forceinline__ uint32_t xmin_pair(float xmin) {
+    if constexpr (DT == FG_DTYPE_BF16) {
+        const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_ru(xmin));
+        return h | (h << 16);
+    } else if constexpr (DT == FG_DTYPE_F16) {
+        const uint32_t h = __half_as_ushort(__float2half_ru(xmin));
+        return h | (h << 16);
+    } else {
+        return 0u;
+    }
+}
+
 // z += sum_e 2^(x_e * c - zmc) over every element of the chunks (two accumulators).
 template <int DT>
 __device__ __forceinline__ void chunks_sumexp(const uint4 (&v)[CPT], float c, float nzmc, float& z0, float& z1) {
@@ -414,7 +453,8 @@ __device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t
 // be compacted before the next window (it passed `limit`, or the next tile
 // could overflow it at twice this window's append rate). Sets st.base to the
 // count and rate2 to twice this window's appends.
-__device__ __forceinline__ bool window_end(uint32_t a_ctl, int tid, Stream& st, uint32_t limit, uint64_t& rate2) {
+__device__ __forceinline__ bool window_end(uint32_t a_ctl, int tid, Stream& st, uint32_t limit, uint32_t kcap,
+                                           uint64_t& rate2) {
     csync();
     const uint32_t slot = st.win % 3u;
     const uint32_t n = st.base + lds_u32(a_ctl + (uint32_t)offsetof(RowCtl, wcnt) + 4u * slot);
@@ -429,7 +469,7 @@ __device__ __forceinline__ bool window_end(uint32_t a_ctl, int tid, Stream& st, 
     st.base = n;
     if (!st.cand) return false;
     if (ovf) { st.cand = false; return false; }
-    return n > limit || (uint64_t)n + rate2 + 64ull > (uint64_t)CAND_CAP;
+    return n > limit || n > kcap || (uint64_t)n + rate2 + 64ull > (uint64_t)CAND_CAP;
 }
 // Tiles (a power of two <= span_max) the next window may cover with n
 // candidates at rate2 / span appends per tile.
@@ -509,7 +549,7 @@ __device__ __forceinline__ void for_row(const KParams& P, const Smem& s, const R
     }
     // RUN chunks per thread are loaded before any is processed, so a pass over
     // a row re-read from L2 keeps RUN * NCT * 16 bytes in flight per CTA.
-    constexpr int RUN = 4;
+    constexpr int RUN = 1;
     const int64_t nchunk = g.interior_bytes / 16;
     const uint4* base = reinterpret_cast<const uint4*>(g.interior);
     for (int64_t ch0 = 0; ch0 < nchunk; ch0 += (int64_t)NCT * RUN) {
@@ -1497,6 +1537,8 @@ struct TileCtx {
     int last_chk, next_chk;   // tile of the last window end, tile of the next
     int span;                 // tiles in the window that just ended
     uint64_t rate2;           // twice the appends of that window
+    uint32_t kcap;            // compact once the buffer holds more than this: the
+                              // threshold then follows the K-th largest so far
 };
 
 // One streamed tile: history mask, max, sum-exp, candidate filter, window
@@ -1582,14 +1624,11 @@ __device__ __forceinline__ bool process_tile(const KParams& P, const RowParams& 
         }
         uint32_t pick = 0;
         if (m >= st.xmin) {
+            const uint32_t x2 = xmin_pair<DT>(st.xmin);
 #pragma unroll
             for (int j = 0; j < CPT; ++j) {
                 const int ch = tid + j * NCT;
-                if (ch < nch) {
-#pragma unroll
-                    for (int e = 0; e < VEC; ++e)
-                        if (!((hb[j] >> e) & 1u) && elem_get<DT>(v[j], e) >= st.xmin) pick |= 1u << (j * VEC + e);
-                }
+                if (ch < nch) pick |= (chunk_ge<DT>(v[j], st.xmin, x2) & ~hb[j]) << (j * VEC);
             }
         }
         while (pick) {
@@ -1619,7 +1658,7 @@ __device__ __forceinline__ bool process_tile(const KParams& P, const RowParams& 
         // last tile; appends are bounds checked, an overflow sends the row
         // to the multi-pass path
         if (t == tc.next_chk || t == g.ntiles - 1) {
-            const bool need = window_end(a_ctl, tid, st, (uint32_t)HWM, tc.rate2);
+            const bool need = window_end(a_ctl, tid, st, (uint32_t)HWM, tc.kcap, tc.rate2);
             tc.span = t - tc.last_chk;
             tc.last_chk = t;
             if (need) return true;   // the caller compacts, then schedules the next window
@@ -1639,6 +1678,7 @@ __device__ __forceinline__ void compact_window(const KParams& P, const int tid, 
     st.klo = max(st.klo, fkey(st.xmin));
     st.base = n;
     if (n > (uint32_t)HWM) st.cand = false;
+    if (2u * n > tc.kcap) tc.kcap = 2u * n;   // ties at the K-th value: do not compact every window
     tc.next_chk = t + window_span(n, tc.rate2, tc.span, span_max_at(t));
 }
 
@@ -1706,7 +1746,7 @@ __device__ void sample_row(const KParams& P, const int tid, const int r, RingPos
 
     {
         const RowGeom gg = row_geom<ESZ>(P, r);
-        TileCtx tc{-1, 0, 1, 0ull};
+        TileCtx tc{-1, 0, 1, 0ull, (uint32_t)max(4 * p.K, 256)};
         if (gg.ntiles > 0) first_tile<DT>(P, tid, r, rp, st, U, tc);
         for (int t = 1; t < gg.ntiles;) {
             bool need;
