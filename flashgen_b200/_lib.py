@@ -21,12 +21,13 @@ FG_ROW_BAD_HISTORY = 0x0008
 FG_ROW_BAD_PARAM = 0x0010
 FG_ROW_BAD_UNIFORM = 0x0020
 FG_ROW_TIMEOUT = 0x0040
+FG_ROW_CAND_TRUNC = 0x0080
 FG_ROW_ERROR_MASK = 0x00FF
 FG_ROW_GENERAL_PATH = 0x0100
 FG_ROW_GREEDY = 0x0200
 
-EXPORTED_SYMBOLS = ("fg_sample", "fg_sample_noalloc", "fg_apply_repetition_penalty", "fg_argmax", "fg_strerror",
-                    "fg_version")
+EXPORTED_SYMBOLS = ("fg_sample", "fg_sample_candidates", "fg_sample_noalloc", "fg_apply_repetition_penalty",
+                    "fg_argmax", "fg_strerror", "fg_version")
 
 
 class FgSampleArgs(ctypes.Structure):
@@ -85,6 +86,9 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib = ctypes.CDLL(path)
         lib.fg_sample.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p]
         lib.fg_sample.restype = ctypes.c_int
+        lib.fg_sample_candidates.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
+        lib.fg_sample_candidates.restype = ctypes.c_int
         lib.fg_sample_noalloc.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p]
         lib.fg_sample_noalloc.restype = ctypes.c_int
         lib.fg_apply_repetition_penalty.argtypes = [

@@ -87,7 +87,12 @@ const char* fg_strerror(int code) {
     }
 }
 
-int fg_sample(const FgSampleArgs* a, void* stream) {
+}  // extern "C"
+
+namespace {
+// fg_sample's launch; the candidate outputs are non-null only for
+// fg_sample_candidates.
+int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* cids, int32_t* ccount, int32_t cmax) {
     if (a == nullptr) return FG_EINVAL;
     const int esz = elem_size(a->dtype);
     if (esz == 0 || a->logits == nullptr || a->batch < 0 || a->vocab < 1) return FG_EINVAL;
@@ -108,6 +113,7 @@ int fg_sample(const FgSampleArgs* a, void* stream) {
     if (rc != FG_OK) return rc;
 
     fg::KParams P{};
+    P.cand_vals = cvals; P.cand_ids = cids; P.cand_count = ccount; P.cand_max = cmax;
     P.logits = a->logits; P.row_stride = a->row_stride; P.batch = a->batch; P.vocab = a->vocab;
     P.vocab_offset = a->vocab_offset; P.vocab_total = vtot;
     P.hist_ids = a->hist_ids; P.hist_offsets = a->hist_offsets;
@@ -170,6 +176,19 @@ int fg_sample(const FgSampleArgs* a, void* stream) {
         case FG_DTYPE_F16: return launch_sample<FG_DTYPE_F16>(P, smem, grid, st, d);
         default: return launch_sample<FG_DTYPE_BF16>(P, smem, grid, st, d);
     }
+}
+}  // namespace
+
+extern "C" {
+
+int fg_sample(const FgSampleArgs* a, void* stream) {
+    return sample_launch(a, stream, nullptr, nullptr, nullptr, 0);
+}
+
+int fg_sample_candidates(const FgSampleArgs* a, float* vals, int32_t* gids, int32_t* counts, int32_t cand_max,
+                         void* stream) {
+    if (vals == nullptr || gids == nullptr || counts == nullptr || cand_max < 1) return FG_EINVAL;
+    return sample_launch(a, stream, vals, gids, counts, cand_max);
 }
 
 // ---------------------------------------------------------------------------

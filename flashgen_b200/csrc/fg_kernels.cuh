@@ -1260,6 +1260,18 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
         }
         best = cons_min_u32(best, s, tid);
         out_id = best;
+        if (P.cand_vals != nullptr) {
+            // candidates mode: the shard's first maximum (the merge takes the
+            // first maximum over the shards' ones, in global-id order)
+            float* cv = P.cand_vals + (int64_t)r * P.cand_max;
+            int32_t* cg = P.cand_ids + (int64_t)r * P.cand_max;
+            const bool any = best != 0xffffffffu;
+            for (int i = tid; i < P.cand_max; i += NCT) {
+                cv[i] = (i == 0 && any) ? M : -INFINITY;
+                cg[i] = (i == 0 && any) ? (int32_t)(best + P.vocab_offset) : INT32_MAX;
+            }
+            if (tid == 0) P.cand_count[r] = any ? 1 : 0;
+        }
         if (pr) for (int c = tid; c < P.vocab; c += NCT) pr[c] = (c == (int)best) ? 1.0f : 0.0f;
     } else if (M != M) {
         status |= FG_ROW_NAN;
@@ -1308,6 +1320,37 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
             }
         }
         auto keepk = [&](uint32_t yk) { return p.mode != MODE_TOPK || yk >= ykK; };
+        if (P.cand_vals != nullptr) {
+            // candidates mode (a vocabulary shard): the row's top-k set, ties
+            // included, as (y, global id); the draw happens after the merge
+            if (p.mode != MODE_TOPK) {
+                status |= FG_ROW_BAD_PARAM;   // top-k off needs the whole distribution
+            } else {
+                if (tid == 0) ctl->ncol = 0u;
+                csync();
+                float* cv = P.cand_vals + (int64_t)r * P.cand_max;
+                int32_t* cg = P.cand_ids + (int64_t)r * P.cand_max;
+                auto put = [&](uint32_t yk, uint32_t col) {
+                    const uint32_t pos = atomicAdd(&ctl->ncol, 1u);
+                    if (pos < (uint32_t)P.cand_max) { cv[pos] = funkey(yk); cg[pos] = (int32_t)(col + P.vocab_offset); }
+                };
+                if (nC > 0) {
+                    for (uint32_t i = tid; i < nC; i += NCT) if (s.ckey[i] >= ykK) put(s.ckey[i], s.cid[i]);
+                } else {
+                    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+                        if (!valid || !(x == x)) return;
+                        const uint32_t yk = fkey(ydiv(p, x));
+                        if (yk >= ykK) put(yk, (uint32_t)c);
+                    });
+                }
+                csync();
+                const uint32_t cnt = ctl->ncol;
+                if (cnt > (uint32_t)P.cand_max) status |= FG_ROW_CAND_TRUNC;
+                const uint32_t w = min(cnt, (uint32_t)P.cand_max);
+                for (uint32_t i = w + tid; i < (uint32_t)P.cand_max; i += NCT) { cv[i] = -INFINITY; cg[i] = INT32_MAX; }
+                if (tid == 0) P.cand_count[r] = (int32_t)w;
+            }
+        } else {
         uint64_t loc = 0;
         for (uint32_t i = tid; i < nC; i += NCT) if (keepk(s.ckey[i])) loc += qC(s.ckey[i]);
         const uint64_t AC = cons_sum_u64(loc, s, tid);   // exact mass of the kept part of C
@@ -1444,6 +1487,7 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
                 pr[c] = val;
             });
         }
+        }   // end of the sampling decision (not run in candidates mode)
     }
     if (pr && out_id < 0) for (int c = tid; c < P.vocab; c += NCT) pr[c] = 0.0f;
     if (tid == 0) {

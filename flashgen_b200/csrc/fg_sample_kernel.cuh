@@ -66,6 +66,11 @@ struct KParams {
     int32_t* out_status;
     float* out_probs;
     Workspace* ws;
+    // candidates mode (vocabulary shards): per row, up to cand_max (y, global id)
+    float* cand_vals;
+    int32_t* cand_ids;
+    int32_t* cand_count;
+    int32_t cand_max;
     // shared-memory layout (byte offsets into dynamic smem)
     int32_t nstage;
     int32_t nwords;          // history bitmap words

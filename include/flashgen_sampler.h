@@ -57,6 +57,8 @@ extern "C" {
 #define FG_ROW_BAD_PARAM    0x0010 /* temperature < 0, top_p outside (0,1], NaN (-1) */
 #define FG_ROW_BAD_UNIFORM  0x0020 /* uniform outside [0,1) or NaN (id = -1)        */
 #define FG_ROW_TIMEOUT      0x0040 /* an on-chip pipeline wait gave up (id = -1)    */
+#define FG_ROW_CAND_TRUNC   0x0080 /* candidates mode: the top-k set (with ties) did
+                                      not fit in cand_max                        */
 #define FG_ROW_ERROR_MASK   0x00FF /* conditions under which FlashGen's sampler
                                       raises (torch indexing / multinomial)      */
 /* informational bits (the id is valid) */
@@ -140,6 +142,26 @@ typedef struct FgSampleArgs {
  * `stream` is a cudaStream_t (NULL = legacy default stream).
  */
 int fg_sample(const FgSampleArgs* args, void* stream);
+
+/*
+ * Local stage of vocabulary-sharded sampling (tensor-parallel LM heads).
+ * `args` describes one shard: columns [vocab_offset, vocab_offset + vocab) of
+ * a vocabulary of vocab_total ids; history ids are global and only the
+ * shard's own columns are penalised. Instead of drawing, each row writes its
+ * top-k set after penalties and temperature: every element whose value y
+ * (= penalised logit / T) is at least the shard's k-th largest, ties
+ * included, as vals[r*cand_max + i] = y and gids[...] = global id, i <
+ * counts[r]; unused slots hold -inf / INT32_MAX. Greedy rows write their
+ * first maximum (y = penalised logit). Rows with top-k off get
+ * FG_ROW_BAD_PARAM (the full distribution would be needed); a top-k set
+ * larger than cand_max gets FG_ROW_CAND_TRUNC. out_ids is written with the
+ * greedy id or -1. The owner of a row merges the shards' sets — top-k of the
+ * union equals the global top-k — and draws with fg_sample on them
+ * (flashgen_b200.sampling.sharded). Replaces the top-k half of
+ * Sampler._sample_one (flashgen/sampling/sampler.py:110-117) on a shard.
+ */
+int fg_sample_candidates(const FgSampleArgs* args, float* vals, int32_t* gids,
+                         int32_t* counts, int32_t cand_max, void* stream);
 
 /*
  * fg_sample without a caller workspace: args->workspace must be NULL, and the
