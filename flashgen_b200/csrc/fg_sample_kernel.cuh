@@ -273,8 +273,9 @@ __device__ __forceinline__ RowParams row_params(const KParams& P, int r) {
 // row after the stream (sampling rows whose top-k is off or above the
 // candidate limit), entries [B, 2B) the other rows, so the long rows start
 // first. Each entry belongs to the half that owns its row; a producer claims
-// ROW_CLAIM entries per atomic.
-constexpr int ROW_CLAIM = 4;
+// ROW_CLAIM entries per atomic. One: a claim of several entries could give one
+// CTA two long rows to run back to back while other CTAs have none.
+constexpr int ROW_CLAIM = 1;
 __device__ __forceinline__ bool row_heavy(const KParams& P, int r) {
     const float T = __ldg(P.temperature + r);
     const bool g = P.greedy ? (__ldg(P.greedy + r) != 0) : false;
