@@ -196,9 +196,15 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
     for (int w = tid; w < nw; w += NCT) s.bitmap[w] = 0u;
     csync();
     const int64_t h0 = __ldg(P.hist_offsets + r), h1 = __ldg(P.hist_offsets + r + 1);
-    constexpr int HB = 4;   // ids per thread per batch, loaded together
+    constexpr int HB = 4;        // ids per thread per batch, loaded together
+    constexpr int HOWN = 4 * HB; // first-setters remembered in registers (histories <= NCT * HOWN)
     int bad = 0;
-    for (int64_t b0 = h0; b0 < h1; b0 += (int64_t)NCT * HB) {
+    // the thread whose atomicOr sets a column's bit first owns the column: it
+    // writes the column's entry of the ascending list once the ranks are known
+    uint32_t own_col[HOWN];
+    uint32_t owned = 0u;
+    int bi = 0;
+    for (int64_t b0 = h0; b0 < h1; b0 += (int64_t)NCT * HB, ++bi) {
         int32_t ids[HB];
 #pragma unroll
         for (int j = 0; j < HB; ++j) {
@@ -214,10 +220,19 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
             const int64_t c = gid - P.vocab_offset;
             if (c >= 0 && c < P.vocab) {
                 const uint32_t bit = 1u << (c & 31);
-                if (!(s.bitmap[c >> 5] & bit)) atomicOr(&s.bitmap[c >> 5], bit);
+                if (!(s.bitmap[c >> 5] & bit)) {
+                    const uint32_t old = atomicOr(&s.bitmap[c >> 5], bit);
+                    if (!(old & bit) && bi * HB + j < HOWN) {
+#pragma unroll
+                        for (int q = 0; q < HOWN; ++q)
+                            if (q == bi * HB + j) own_col[q] = (uint32_t)c;
+                        owned |= 1u << (bi * HB + j);
+                    }
+                }
             }
         }
     }
+    const bool own_all = (h1 - h0) <= (int64_t)NCT * HOWN;
     if (bad) atomicOr(&s.ctl->status, FG_ROW_BAD_HISTORY);
     csync();
     // popcount prefix per 64-column pair of words, in pair order: warp w owns
@@ -251,16 +266,27 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
         run += __shfl_sync(0xffffffffu, incl, 31);
     }
     csync();
-    // ascending list of distinct columns: words strided over the threads
-    for (int w = tid; w < nw; w += NCT) {
-        uint32_t bits = s.bitmap[w];
-        if (bits == 0u) continue;
-        uint32_t rk = hist_rank(s, (uint32_t)(w * 32));
-        while (bits) {
-            const int b = __ffs(bits) - 1;
-            bits &= bits - 1;
-            if (rk < cap) s.scol[rk] = (uint32_t)(w * 32 + b);
-            ++rk;
+    // ascending list of distinct columns: each owner writes its columns' entries
+    // (histories longer than NCT * HOWN: words strided over the threads)
+    if (own_all) {
+#pragma unroll
+        for (int q = 0; q < HOWN; ++q) {
+            if ((owned >> q) & 1u) {
+                const uint32_t rk = hist_rank(s, own_col[q]);
+                if (rk < cap) s.scol[rk] = own_col[q];
+            }
+        }
+    } else {
+        for (int w = tid; w < nw; w += NCT) {
+            uint32_t bits = s.bitmap[w];
+            if (bits == 0u) continue;
+            uint32_t rk = hist_rank(s, (uint32_t)(w * 32));
+            while (bits) {
+                const int b = __ffs(bits) - 1;
+                bits &= bits - 1;
+                if (rk < cap) s.scol[rk] = (uint32_t)(w * 32 + b);
+                ++rk;
+            }
         }
     }
     const uint32_t U = min(total, cap);
