@@ -1141,6 +1141,18 @@ __device__ uint32_t jth_id_row(const KParams& P, const Smem& s, const RowParams&
 // ---------------------------------------------------------------------------
 // Producer warp (one elected lane): row queue + bulk copies into the ring
 // ---------------------------------------------------------------------------
+// Bounded wait until *go reaches `want`; false on abort or after WAIT_LIMIT_NS.
+__device__ __forceinline__ bool wait_go(volatile uint32_t* go, uint32_t want, volatile int* abort) {
+    if (*go >= want) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (*go < want) {
+        if (*abort) return false;
+        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) return false;
+        __nanosleep(64);
+    }
+    return true;
+}
+
 template <int DT>
 __device__ void producer(const KParams& P, const Smem& s) {
     constexpr int ESZ = Elem<DT>::SIZE;
@@ -1185,6 +1197,7 @@ __device__ void producer(const KParams& P, const Smem& s) {
         while (hpos < nheld) mark(held[hpos++]);   // claimed, never published
         drain();
     };
+    uint32_t nrow = 0;
     int e = fetch();
     while (true) {
         const uint32_t slot = k % RQ, rph = (k / RQ) & 1u;
@@ -1198,10 +1211,8 @@ __device__ void producer(const KParams& P, const Smem& s) {
         // consumers release them (sample_row returns them to normal priority)
         const bool keep = (e & HEAVY) != 0;
         const RowGeom g = row_geom<ESZ>(P, rcur);
-        int en = -2;   // next entry, looked up once the ring is full
         for (int t = 0; t < g.ntiles; ++t, ++it) {
-            if (en == -2 && !mbar_test(&s.empty[st], ph ^ 1u)) en = fetch();
-            if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) { give_up(en); return; }
+            if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) { give_up(-1); return; }
             const int64_t off = (int64_t)t * TILE_BYTES;
             const int64_t left = g.interior_bytes - off;
             const uint32_t bytes = (uint32_t)(left < TILE_BYTES ? left : TILE_BYTES);
@@ -1210,8 +1221,13 @@ __device__ void producer(const KParams& P, const Smem& s) {
             else bulk_g2s(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st]);
             if (++st == ns) { st = 0; ph ^= 1u; }
         }
-        if (en == -2) en = fetch();
-        e = en;
+        // The next row is claimed only when the consumers allow it: after this
+        // row's stream, or after its passes over the row when it may need
+        // some. A row claimed earlier would wait behind this one while other
+        // CTAs run out of rows.
+        ++nrow;
+        if (!wait_go(&s.ctl->go, nrow, abort)) { give_up(-1); return; }
+        e = fetch();
     }
 }
 
@@ -1789,6 +1805,11 @@ __device__ __noinline__ int stream_row(const KParams& P, const int tid, const in
     return t;
 }
 
+__device__ __forceinline__ void release_claim(const KParams& P) {
+    volatile uint32_t* go = &carve(smem_base(), P).ctl->go;
+    *go = *go + 1u;
+}
+
 template <int DT>
 __device__ void sample_row(const KParams& P, const int tid, const int r, RingPos& rp) {
     using E = Elem<DT>;
@@ -1824,6 +1845,10 @@ __device__ void sample_row(const KParams& P, const int tid, const int r, RingPos
             if (need) compact_window(P, tid, r, t - 1, st, tc, DT == FG_DTYPE_F32 ? 0 : DT);
         }
     }
+    // every tile of the row has been taken from the ring; a row without
+    // passes over it after the stream lets the producer claim the next row now
+    const bool heavy = row_heavy(P, r);
+    if (tid == 0 && !heavy) release_claim(P);
 
     const Smem s = carve(smem_base(), P);
     RowCtl* ctl = s.ctl;
@@ -1868,7 +1893,8 @@ __device__ void sample_row(const KParams& P, const int tid, const int r, RingPos
 
     finish_row_cold<DT>(P, tid, r, st.tmax, st.tmin, st.z0, st.z1, st.nzmc, st.cand, st.base, st.imax, st.itile,
                         st.bestv, st.bestc, aborted);
-    if (row_heavy(P, r)) {
+    if (tid == 0 && heavy) release_claim(P);
+    if (heavy) {
         // the producer streamed this row with an evict-last policy: release it
         const uintptr_t a0 = reinterpret_cast<uintptr_t>(g.interior) & ~uintptr_t(127);
         const uintptr_t a1 = reinterpret_cast<uintptr_t>(g.interior) + (uintptr_t)g.interior_bytes;
@@ -1943,6 +1969,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) fg_sample_kernel(const __grid_con
         for (int i = 0; i < P.nstage; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], NCW); }
         for (int i = 0; i < RQ; ++i) { mbar_init(&s.rowfull[i], 1); mbar_init(&s.rowempty[i], 1); }
         s.ctl->abort = 0;
+        s.ctl->go = 0u;
         fence_mbar_init();
     }
     __syncthreads();

@@ -100,6 +100,7 @@ struct RowCtl {
     uint32_t nunique;        // unique history columns in this call's range
     uint32_t snap;
     uint32_t ncol;           // collected entries (multi-pass paths)
+    uint32_t go;             // rows after which the consumers let the producer claim the next one
     SelSlot sel[2];          // select results, alternating between passes
 };
 
