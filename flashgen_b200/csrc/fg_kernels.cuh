@@ -1251,8 +1251,10 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
     // ---- row statistics ----
     const float M = cons_max_nan(st.tmax, s, tid);
     int status = ctl->status;
-    const bool cand_ok = st.cand && !aborted;
     const uint32_t n = st.base;
+    // a top-k row whose filter (started from a sample of the row) kept fewer
+    // than K elements runs its select over the whole row
+    const bool cand_ok = st.cand && !aborted && (p.mode != MODE_TOPK || n >= (uint32_t)p.K);
     double Zq = 0.0;
     float My = M;
     float ymin = -INFINITY;
@@ -1552,12 +1554,20 @@ __device__ __forceinline__ void tau0_cold(const KParams& P, int tid, int r, uint
     const uint4 v[CPT] = {v0, v1};
     // starting threshold from the first tile: the K-th largest of
     // disjoint group maxima (thread maxima for K <= NCT/2, chunk
-    // maxima for K <= NCT, elements otherwise) bounds the row's K-th
-    // largest from below
+    // maxima for K <= NCT, elements otherwise) of the tile. With K the
+    // tile's share of the row's candidate target (1.5x, plus 8) rather than
+    // the target itself, the filter passes about 1.5 target's worth of the
+    // row on rows whose values are spread evenly along it, instead of every
+    // tile's top K. The end of the row checks that the filter kept enough:
+    // at least the row's top_k for top-k rows, enough mass for the nucleus
+    // otherwise; a row that fails takes the whole-row path.
     float cm[CPT];
 #pragma unroll
     for (int j = 0; j < CPT; ++j) cm[j] = chunk_max1<DT>(v[j]);
-    const int K = p.K;
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    const int64_t n0 = (g.interior_bytes < TILE_BYTES ? g.interior_bytes : TILE_BYTES) / Elem<DT>::SIZE;
+    const int share = (int)ceilf(1.5f * (float)p.K * (float)n0 / (float)P.vocab) + 8;
+    const int K = max(1, min(p.K, share));
     // key range of the values the select will see
     float lo_v = INFINITY;
     if (K <= NCT / 2) lo_v = m;

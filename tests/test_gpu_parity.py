@@ -132,6 +132,24 @@ def test_large_top_k_general_path(cuda_device):
     assert (status & _lib.FG_ROW_GENERAL_PATH).all()
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_sorted_rows(cuda_device, dtype):
+    # The candidate filter starts from a sample of the row's first tile. On
+    # rows sorted in descending order that sample holds the row's largest
+    # values, so a row with a large K keeps fewer than K elements and must
+    # take the whole-row select; ascending rows start from the row's smallest
+    # values.
+    g = torch.Generator().manual_seed(11)
+    B, V = 8, 128256
+    x = torch.randn(B, V, generator=g)
+    x[:4] = torch.sort(x[:4], dim=1, descending=True).values
+    x[4:] = torch.sort(x[4:], dim=1).values
+    p = BatchParams.uniform(B, temperature=0.9, top_p=0.95, top_k=-1)
+    p.top_k[:] = [20, 1000, 0, 100, 20, 1000, 0, 100]
+    stats, ids, status = _check(_workload(x.to(dtype), p, seed=3))
+    assert status[1] & _lib.FG_ROW_GENERAL_PATH
+
+
 def test_penalties_all_kinds(cuda_device):
     rng = np.random.default_rng(2)
     B, V = 16, 40000
