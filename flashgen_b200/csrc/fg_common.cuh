@@ -197,6 +197,27 @@ __device__ __forceinline__ bool mbar_test_a(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ void mbar_arrive_a(uint32_t bar) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" :: "r"(bar) : "memory");
 }
+// Shared-memory atomics on generic pointers into the dynamic shared memory.
+// The pointers come from an opaque base, so a plain atomicAdd would compile to
+// a generic atomic, which serialises far more under contention than the
+// shared-window form used here.
+__device__ __forceinline__ uint32_t atoms_add(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.shared.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(smem_u32(p)), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void reds_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.shared.add.u32 [%0], %1;" :: "r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atoms_or(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.shared.or.b32 %0, [%1], %2;" : "=r"(old) : "r"(smem_u32(p)), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void reds_or(uint32_t* p, uint32_t v) {
+    asm volatile("red.shared.or.b32 [%0], %1;" :: "r"(smem_u32(p)), "r"(v) : "memory");
+}
+
 // mbar_wait on a shared-window address; the abort flag is the int at `abort_a`.
 __device__ __forceinline__ bool mbar_wait_a(uint32_t bar, uint32_t parity, uint32_t abort_a) {
     if (mbar_test_a(bar, parity)) return true;

@@ -221,7 +221,7 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
             if (c >= 0 && c < P.vocab) {
                 const uint32_t bit = 1u << (c & 31);
                 if (!(s.bitmap[c >> 5] & bit)) {
-                    const uint32_t old = atomicOr(&s.bitmap[c >> 5], bit);
+                    const uint32_t old = atoms_or(&s.bitmap[c >> 5], bit);
                     if (!(old & bit) && bi * HB + j < HOWN) {
 #pragma unroll
                         for (int q = 0; q < HOWN; ++q)
@@ -233,7 +233,7 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
         }
     }
     const bool own_all = (h1 - h0) <= (int64_t)NCT * HOWN;
-    if (bad) atomicOr(&s.ctl->status, FG_ROW_BAD_HISTORY);
+    if (bad) reds_or(reinterpret_cast<uint32_t*>(&s.ctl->status), (uint32_t)FG_ROW_BAD_HISTORY);
     csync();
     // popcount prefix per 64-column pair of words, in pair order: warp w owns
     // pairs [w * ppw, (w + 1) * ppw), its lanes take 32 consecutive pairs at a
@@ -292,7 +292,7 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
     const uint32_t U = min(total, cap);
     if (tid == 0) {
         s.ctl->nunique = U;
-        if (total > cap || total > 65535u) atomicOr(&s.ctl->status, FG_ROW_BAD_PARAM);
+        if (total > cap || total > 65535u) reds_or(reinterpret_cast<uint32_t*>(&s.ctl->status), (uint32_t)FG_ROW_BAD_PARAM);
     }
     for (uint32_t i = tid; i < U; i += NCT) s.sval[i] = -INFINITY;
     if (p.freq_on) {
@@ -313,7 +313,7 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
                 bool v = i < h1 && gid >= 0 && gid < P.vocab_total && c >= 0 && c < P.vocab;
                 const uint32_t rk = v ? hist_rank(s, (uint32_t)c) : 0u;
                 v = v && rk < U;
-                if (v) atomicAdd(&s.counts[rk], 1u);
+                if (v) reds_add(&s.counts[rk], 1u);
             }
         }
     }
@@ -359,7 +359,7 @@ struct Stream {
 // and reduced only when a compaction needs it.
 __device__ __forceinline__ void append1(const Smem& s, Stream& st, uint32_t key, uint32_t col) {
     const int slot = (int)(st.win % 3u);
-    const uint32_t pos = st.base + atomicAdd(&s.ctl->wcnt[slot], 1u);
+    const uint32_t pos = st.base + atoms_add(&s.ctl->wcnt[slot], 1u);
     if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = key; s.cid[pos] = col; } else s.ctl->ovf[slot] = 1;
     st.khi = max(st.khi, key); st.klo = min(st.klo, key);
 }
@@ -465,7 +465,7 @@ __device__ uint32_t compact(const RowParams& p, const Smem& s, int tid, uint32_t
     const int lane = tid & 31;
     const uint32_t incl = warp_incl_scan_u32(cnt, lane);
     uint32_t base = 0;
-    if (lane == 31) base = atomicAdd(&ctl->ncol, incl);
+    if (lane == 31) base = atoms_add(&ctl->ncol, incl);
     base = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
 #pragma unroll
     for (int j = 0; j < PER; ++j)
@@ -573,47 +573,62 @@ __device__ __forceinline__ void for_row(const KParams& P, const Smem& s, const R
         }
         f(valid, valid ? c : 0, x);
     }
-    // RUN chunks per thread are loaded before any is processed, so a pass over
-    // a row re-read from L2 keeps RUN * NCT * 16 bytes in flight per CTA.
-    constexpr int RUN = 1;
-    const int64_t nchunk = g.interior_bytes / 16;
-    const uint4* base = reinterpret_cast<const uint4*>(g.interior);
-    for (int64_t ch0 = 0; ch0 < nchunk; ch0 += (int64_t)NCT * RUN) {
-      uint4 vr[RUN];
+    // The interior comes through the ring: the producer streams the row once
+    // more for each request (from L2, where rows that may need passes are kept
+    // with an evict-last policy), with the copies of several tiles in flight.
+    RowCtl* ctl = s.ctl;
+    volatile int* abort = &ctl->abort;
+    const uint32_t ns = (uint32_t)P.nstage;
+    uint32_t st = ctl->rst, ph = ctl->rph;
+    csync();   // every thread has the position before it moves
+    if (tid == 0) { volatile uint32_t* q = &ctl->preq; *q = *q + 1u; }
+    const int lane = tid & 31;
+    for (int t = 0; t < g.ntiles; ++t) {
+        const bool ok = mbar_wait(&s.full[st], ph, abort);
+        if (!ok) *abort = 1;
+        const int64_t left = g.interior_bytes - (int64_t)t * TILE_BYTES;
+        const int nch = ok ? (int)((left < TILE_BYTES ? left : TILE_BYTES) / 16) : 0;
+        const uint8_t* tile = s.ring + (int64_t)st * TILE_BYTES;
+        uint4 v[CPT];
 #pragma unroll
-      for (int u = 0; u < RUN; ++u) {
-          const int64_t ch = ch0 + tid + (int64_t)u * NCT;
-          vr[u] = ch < nchunk ? __ldg(base + ch) : make_uint4(0u, 0u, 0u, 0u);
-      }
-#pragma unroll
-      for (int u = 0; u < RUN; ++u) {
-        const int64_t ch = ch0 + tid + (int64_t)u * NCT;
-        const bool valid = ch < nchunk;
-        float x[VEC];
-        int c0 = 0;
-        if (valid) {
-            const uint4 v = vr[u];
-            E::unpack(v, x);
-            c0 = g.head + (int)(ch * VEC);
-            if (p.pen) {
-                uint32_t bits = hist_bits(s, P.nwords, c0, VEC);
-                while (bits) {
-                    const int e = __ffs(bits) - 1;
-                    bits &= bits - 1;
-                    const uint32_t rk = hist_rank(s, (uint32_t)(c0 + e));
-#pragma unroll
-                    for (int j = 0; j < VEC; ++j)
-                        if (j == e) x[j] = penalize(p, s, rk, x[j]);
-                }
-            }
-        } else {
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) x[e] = -INFINITY;
+        for (int j = 0; j < CPT; ++j) {
+            const int ch = tid + j * NCT;
+            v[j] = ch < nch ? *reinterpret_cast<const uint4*>(tile + (int64_t)ch * 16) : make_uint4(0u, 0u, 0u, 0u);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[st]);
+        if (++st == ns) { st = 0; ph ^= 1u; }
+        const int tcol0 = g.head + t * (TILE_BYTES / ESZ);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) f(valid, c0 + e, x[e]);
-      }
+        for (int j = 0; j < CPT; ++j) {
+            const int ch = tid + j * NCT;
+            const bool valid = ch < nch;
+            float x[VEC];
+            const int c0 = tcol0 + ch * VEC;
+            if (valid) {
+                E::unpack(v[j], x);
+                if (p.pen) {
+                    uint32_t bits = hist_bits(s, P.nwords, c0, VEC);
+                    while (bits) {
+                        const int e = __ffs(bits) - 1;
+                        bits &= bits - 1;
+                        const uint32_t rk = hist_rank(s, (uint32_t)(c0 + e));
+#pragma unroll
+                        for (int q = 0; q < VEC; ++q)
+                            if (q == e) x[q] = penalize(p, s, rk, x[q]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) x[e] = -INFINITY;
+            }
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) f(valid, valid ? c0 + e : 0, x[e]);
+        }
     }
+    csync();   // every thread is past its reads of the position
+    if (tid == 0) { ctl->rst = st; ctl->rph = ph; }
+    csync();
 }
 
 __device__ __forceinline__ uint64_t q_of(float e, float scale) { return (uint64_t)__float2ull_rn(e * scale); }
@@ -743,7 +758,7 @@ __device__ __forceinline__ Located locate(const KParams& P, const Smem& s, const
         const float y = ydiv(p, x);
         const uint32_t k = fkey(y);
         if (valid && k >= rlo && k <= rhi && lbin(y) == b0 && (k & pmask) == prefix) {
-            const uint32_t pos = slot0 + atomicAdd(&s.ctl->ncol, 1u);
+            const uint32_t pos = slot0 + atoms_add(&s.ctl->ncol, 1u);
             if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = k; s.cid[pos] = (uint32_t)c; }
             kmn = min(kmn, k); kmx = max(kmx, k);
         }
@@ -935,7 +950,7 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
         if (d == 0) {
             // nothing lies above level 0's range: counts only
             for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
-                if (valid && x >= a0 && x <= xhi && x >= xlo) atomicAdd(&cnt[wbin(x, a0, bi)], 1u);
+                if (valid && x >= a0 && x <= xhi && x >= xlo) reds_add(&cnt[wbin(x, a0, bi)], 1u);
             });
         } else {
             // branch-free per element: the mass is computed for every element
@@ -944,7 +959,7 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
                 const bool inr = valid && x >= xlo && x <= xhi;
                 const uint64_t q = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
                 acc += (inr && x > a1) ? q : 0ull;
-                if (inr && x <= a1 && x >= a0) atomicAdd(&cnt[wbin(x, a0, bi)], 1u);
+                if (inr && x <= a1 && x >= a0) reds_add(&cnt[wbin(x, a0, bi)], 1u);
             });
         }
         csync();
@@ -1018,7 +1033,7 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
         if (bal) {
             const int lead = __ffs(bal) - 1;
             uint32_t b0 = 0u;
-            if (lane == lead) b0 = atomicAdd(&s.ctl->ncol, (uint32_t)__popc(bal));
+            if (lane == lead) b0 = atoms_add(&s.ctl->ncol, (uint32_t)__popc(bal));
             b0 = __shfl_sync(0xffffffffu, b0, lead);
             if (in) {
                 const uint32_t k = fkey(ydiv(p, x));
@@ -1141,18 +1156,6 @@ __device__ uint32_t jth_id_row(const KParams& P, const Smem& s, const RowParams&
 // ---------------------------------------------------------------------------
 // Producer warp (one elected lane): row queue + bulk copies into the ring
 // ---------------------------------------------------------------------------
-// Bounded wait until *go reaches `want`; false on abort or after WAIT_LIMIT_NS.
-__device__ __forceinline__ bool wait_go(volatile uint32_t* go, uint32_t want, volatile int* abort) {
-    if (*go >= want) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (*go < want) {
-        if (*abort) return false;
-        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) return false;
-        __nanosleep(64);
-    }
-    return true;
-}
-
 template <int DT>
 __device__ void producer(const KParams& P, const Smem& s) {
     constexpr int ESZ = Elem<DT>::SIZE;
@@ -1197,7 +1200,7 @@ __device__ void producer(const KParams& P, const Smem& s) {
         while (hpos < nheld) mark(held[hpos++]);   // claimed, never published
         drain();
     };
-    uint32_t nrow = 0;
+    uint32_t nrow = 0, served = 0;
     int e = fetch();
     while (true) {
         const uint32_t slot = k % RQ, rph = (k / RQ) & 1u;
@@ -1211,22 +1214,42 @@ __device__ void producer(const KParams& P, const Smem& s) {
         // consumers release them (sample_row returns them to normal priority)
         const bool keep = (e & HEAVY) != 0;
         const RowGeom g = row_geom<ESZ>(P, rcur);
-        for (int t = 0; t < g.ntiles; ++t, ++it) {
-            if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) { give_up(-1); return; }
-            const int64_t off = (int64_t)t * TILE_BYTES;
-            const int64_t left = g.interior_bytes - off;
-            const uint32_t bytes = (uint32_t)(left < TILE_BYTES ? left : TILE_BYTES);
-            mbar_arrive_expect_tx(&s.full[st], bytes);
-            if (keep) bulk_g2s_hint(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st], pol_keep);
-            else bulk_g2s(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st]);
-            if (++st == ns) { st = 0; ph ^= 1u; }
-        }
-        // The next row is claimed only when the consumers allow it: after this
-        // row's stream, or after its passes over the row when it may need
-        // some. A row claimed earlier would wait behind this one while other
-        // CTAs run out of rows.
+        // the row's interior, tile by tile, through the ring
+        auto stream = [&]() -> bool {
+            for (int t = 0; t < g.ntiles; ++t, ++it) {
+                if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) return false;
+                const int64_t off = (int64_t)t * TILE_BYTES;
+                const int64_t left = g.interior_bytes - off;
+                const uint32_t bytes = (uint32_t)(left < TILE_BYTES ? left : TILE_BYTES);
+                mbar_arrive_expect_tx(&s.full[st], bytes);
+                if (keep) bulk_g2s_hint(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st], pol_keep);
+                else bulk_g2s(s.ring + (int64_t)st * TILE_BYTES, g.interior + off, bytes, &s.full[st]);
+                if (++st == ns) { st = 0; ph ^= 1u; }
+            }
+            return true;
+        };
+        if (!stream()) { give_up(-1); return; }
+        // Until the consumers release the row, stream it again for each pass
+        // over it that they request (their multi-pass paths read the row
+        // through the ring). The next row is claimed only after the release,
+        // so no claimed row waits behind a long one while other CTAs run out
+        // of rows.
         ++nrow;
-        if (!wait_go(&s.ctl->go, nrow, abort)) { give_up(-1); return; }
+        {
+            volatile uint32_t* go = &s.ctl->go;
+            volatile uint32_t* preq = &s.ctl->preq;
+            uint64_t t0 = globaltimer_ns();
+            while (*go < nrow) {
+                if (*preq != served) {
+                    ++served;
+                    if (!stream()) { give_up(-1); return; }
+                    t0 = globaltimer_ns();
+                    continue;
+                }
+                if (*abort || globaltimer_ns() - t0 > WAIT_LIMIT_NS) { give_up(-1); return; }
+                __nanosleep(64);
+            }
+        }
         e = fetch();
     }
 }
@@ -1375,7 +1398,7 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
                 float* cv = P.cand_vals + (int64_t)r * P.cand_max;
                 int32_t* cg = P.cand_ids + (int64_t)r * P.cand_max;
                 auto put = [&](uint32_t yk, uint32_t col) {
-                    const uint32_t pos = atomicAdd(&ctl->ncol, 1u);
+                    const uint32_t pos = atoms_add(&ctl->ncol, 1u);
                     if (pos < (uint32_t)P.cand_max) { cv[pos] = funkey(yk); cg[pos] = (int32_t)(col + P.vocab_offset); }
                 };
                 if (nC > 0) {
@@ -1855,10 +1878,7 @@ __device__ void sample_row(const KParams& P, const int tid, const int r, RingPos
             if (need) compact_window(P, tid, r, t - 1, st, tc, DT == FG_DTYPE_F32 ? 0 : DT);
         }
     }
-    // every tile of the row has been taken from the ring; a row without
-    // passes over it after the stream lets the producer claim the next row now
     const bool heavy = row_heavy(P, r);
-    if (tid == 0 && !heavy) release_claim(P);
 
     const Smem s = carve(smem_base(), P);
     RowCtl* ctl = s.ctl;
@@ -1896,14 +1916,19 @@ __device__ void sample_row(const KParams& P, const int tid, const int r, RingPos
     }
     // last window: nothing is appended after it, so only the limit applies
     if (st.cand) (void)window_check(P, r, p, s, tid, st, (uint32_t)HWM + (CAND_CAP - HWM) / 2, 1 << 20, 1);
-    // uniform snapshot of the abort flag (the producer may set it at any time)
-    if (tid == 0) ctl->snap = (*abort != 0) ? 1u : 0u;
+    // uniform snapshot of the abort flag (the producer may set it at any time);
+    // the ring position for the passes over the row that the finish may take
+    if (tid == 0) { ctl->snap = (*abort != 0) ? 1u : 0u; ctl->rst = rp.st; ctl->rph = rp.ph; }
     csync();
     const bool aborted = ctl->snap != 0;
 
     finish_row_cold<DT>(P, tid, r, st.tmax, st.tmin, st.z0, st.z1, st.nzmc, st.cand, st.base, st.imax, st.itile,
                         st.bestv, st.bestc, aborted);
-    if (tid == 0 && heavy) release_claim(P);
+    csync();
+    rp.st = ctl->rst;
+    rp.ph = ctl->rph;
+    // the row is done with: the producer may claim the next one
+    if (tid == 0) release_claim(P);
     if (heavy) {
         // the producer streamed this row with an evict-last policy: release it
         const uintptr_t a0 = reinterpret_cast<uintptr_t>(g.interior) & ~uintptr_t(127);
@@ -1980,6 +2005,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) fg_sample_kernel(const __grid_con
         for (int i = 0; i < RQ; ++i) { mbar_init(&s.rowfull[i], 1); mbar_init(&s.rowempty[i], 1); }
         s.ctl->abort = 0;
         s.ctl->go = 0u;
+        s.ctl->preq = 0u;
         fence_mbar_init();
     }
     __syncthreads();

@@ -101,6 +101,8 @@ struct RowCtl {
     uint32_t snap;
     uint32_t ncol;           // collected entries (multi-pass paths)
     uint32_t go;             // rows after which the consumers let the producer claim the next one
+    uint32_t preq;           // passes over the current row requested from the producer
+    uint32_t rst, rph;       // consumers' ring position between passes
     SelSlot sel[2];          // select results, alternating between passes
 };
 
@@ -448,15 +450,15 @@ template <bool COUNT>
 __device__ __forceinline__ void add_bin(uint32_t* cnts, uint32_t* blo, uint32_t* bhi, bool valid, uint32_t d,
                                         uint64_t w) {
     if (!valid) return;
-    atomicAdd(&cnts[d], 1u);
+    reds_add(&cnts[d], 1u);
     if (COUNT || w == 0) return;
     const uint32_t l = (uint32_t)w;
     uint32_t h = (uint32_t)(w >> 32);
     if (l) {
-        const uint32_t old = atomicAdd(&blo[d], l);
+        const uint32_t old = atoms_add(&blo[d], l);
         h += (old + l < old) ? 1u : 0u;
     }
-    if (h) atomicAdd(&bhi[d], h);
+    if (h) reds_add(&bhi[d], h);
 }
 __device__ __forceinline__ uint64_t bin_mass(const uint32_t* blo, const uint32_t* bhi, int d) {
     return ((uint64_t)bhi[d] << 32) | blo[d];
