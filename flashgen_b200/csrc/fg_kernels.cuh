@@ -1260,6 +1260,78 @@ __device__ void producer(const KParams& P, const Smem& s) {
 struct RingPos { uint32_t st, ph; };
 
 // ---------------------------------------------------------------------------
+// Sorted candidate set: the finish of a row whose decision lies inside the
+// candidate buffer. The buffer's (y-key, column) pairs are sorted once, in
+// place, into descending key order with ties in ascending column order (the
+// draw order), so the K-th key, the top-p cut and the draw are positions in
+// one prefix of the sorted array: the first position whose inclusive prefix
+// mass exceeds a target. Same integer masses and the same comparisons as the
+// radix selects they replace, hence the same token. The bitonic sort costs
+// O(n log^2 n) against the selects' few O(n) passes with their fixed costs, so
+// it serves small sets only (the top-k rows with small K).
+// ---------------------------------------------------------------------------
+constexpr uint32_t SORT_MAX = 512;
+__device__ __noinline__ void sort_cands_desc(const KParams& P, int tid, uint32_t n) {
+    const Smem s = carve(smem_base(), P);
+    uint32_t N = 2;
+    while (N < n) N <<= 1;
+    for (uint32_t i = n + tid; i < N; i += NCT) { s.ckey[i] = 0u; s.cid[i] = 0xffffffffu; }
+    csync();
+    for (uint32_t k = 2; k <= N; k <<= 1) {
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            for (uint32_t t = tid; t < N / 2; t += NCT) {
+                const uint32_t i = ((t & ~(j - 1u)) << 1) | (t & (j - 1u));
+                const uint32_t l = i + j;
+                const uint32_t ki = s.ckey[i], kl = s.ckey[l];
+                const uint32_t ii = s.cid[i], il = s.cid[l];
+                const bool first = ki > kl || (ki == kl && ii < il);   // i precedes l in the draw order
+                const bool desc = (i & k) == 0u;
+                if (desc != first) { s.ckey[i] = kl; s.ckey[l] = ki; s.cid[i] = il; s.cid[l] = ii; }
+            }
+            csync();
+        }
+    }
+}
+
+// First position i in [0, lim) of the sorted buffer whose inclusive prefix
+// mass exceeds T (T below the mass of [0, lim)); *incl = that prefix mass.
+__device__ __noinline__ uint32_t sorted_crossing(const KParams& P, int tid, uint32_t lim, uint64_t T, float My,
+                                                float scale, uint64_t* incl) {
+    const Smem s = carve(smem_base(), P);
+    const int lane = tid & 31, wid = tid >> 5;
+    const uint32_t E = (lim + NCT - 1) / NCT;
+    const uint32_t i0 = min(lim, (uint32_t)tid * E), i1 = min(lim, i0 + E);
+    auto q = [&](uint32_t i) { return q_of(expf(funkey(s.ckey[i]) - My), scale); };
+    uint64_t S = 0;
+    for (uint32_t i = i0; i < i1; ++i) S += q(i);
+    // exclusive prefix of the per-thread sums (threads in index order)
+    uint64_t x = S;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t y = shfl_u64(x, (lane - o) & 31);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s.red64[wid] = x;
+    csync();
+    uint64_t base = x - S;
+    for (int w = 0; w < NCW; ++w) if (w < wid) base += s.red64[w];
+    if (tid == 0) { s.ctl->ncol = 0xffffffffu; }
+    csync();
+    if (base <= T && T < base + S) {
+        uint64_t acc = base;
+        for (uint32_t i = i0; i < i1; ++i) {
+            acc += q(i);
+            if (acc > T) { s.ctl->ncol = i; *reinterpret_cast<uint64_t*>(s.redd) = acc; break; }
+        }
+    }
+    csync();
+    const uint32_t r = s.ctl->ncol;
+    *incl = *reinterpret_cast<const uint64_t*>(s.redd);
+    csync();
+    return r;
+}
+
+// ---------------------------------------------------------------------------
 // After the stream: row statistics, the decision (greedy / sampling), outputs.
 // ---------------------------------------------------------------------------
 template <int DT>
@@ -1361,10 +1433,15 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
         const uint32_t cLo = min(loY, hiY);
         const int remC = varying_bits(cLo, hiY);
         auto qC = [&](uint32_t yk) { return q_of(expf(funkey(yk) - My), scale); };   // exact masses in C
+        // the sampling rows' candidate sets are sorted into the draw order
+        const bool sorted = nC > 0 && nC <= SORT_MAX && P.cand_vals == nullptr;
+        if (sorted) sort_cands_desc(P, tid, nC);
         // top-k threshold (on C, or over the whole row when C cannot hold it)
         uint32_t ykK = 0u;
         if (p.mode == MODE_TOPK) {
-            if (cand_ok) {
+            if (cand_ok && sorted) {
+                ykK = s.ckey[p.K - 1];   // nC >= K
+            } else if (cand_ok) {
                 const SelOut so = block_select<true, true>(
                     [&](auto&& f) {
                         for (uint32_t i0 = 0; i0 < nC; i0 += NCT) {
@@ -1418,9 +1495,11 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
                 if (tid == 0) P.cand_count[r] = (int32_t)w;
             }
         } else {
-        uint64_t loc = 0;
-        for (uint32_t i = tid; i < nC; i += NCT) if (keepk(s.ckey[i])) loc += qC(s.ckey[i]);
+        uint64_t loc = 0, nloc = 0;
+        for (uint32_t i = tid; i < nC; i += NCT) if (keepk(s.ckey[i])) { loc += qC(s.ckey[i]); ++nloc; }
         const uint64_t AC = cons_sum_u64(loc, s, tid);   // exact mass of the kept part of C
+        // the kept part of a sorted C is its prefix [0, nk)
+        const uint32_t nk = sorted ? (uint32_t)cons_sum_u64(nloc, s, tid) : 0u;
 
         // region R below C (whole row when C is empty), restricted to y >= T_K for top-k
         const uint32_t rlo = (p.mode == MODE_TOPK) ? ykK : KEY_NEG_INF;
@@ -1439,7 +1518,20 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
             const double Pd = (double)p.top_p * Qn;
             const uint64_t Pt = (uint64_t)floor(Pd);
             cut = true;
-            if ((double)AC > Pd && nC > 0) {
+            if ((double)AC > Pd && nC > 0 && sorted) {
+                uint64_t incl = 0;
+                const uint32_t ic = min(sorted_crossing(P, tid, nk, Pt, My, scale, &incl), nk - 1u);
+                tstar = s.ckey[ic];
+                // the run of entries with key tstar around ic (ties at the cut)
+                uint32_t a = 0xffffffffu, b = 0u;
+                for (uint32_t i = tid; i < nk; i += NCT)
+                    if (s.ckey[i] == tstar) { a = min(a, i); b = max(b, i + 1u); }
+                a = cons_min_u32(a, s, tid);
+                b = cons_max_u32(b, s, tid);
+                n_t = b - a;
+                m_t = ic - a + 1u;
+                Qf = incl;
+            } else if ((double)AC > Pd && nC > 0) {
                 const SelOut so = block_select<true, false>(
                     [&](auto&& f) {
                         for (uint32_t i0 = 0; i0 < nC; i0 += NCT) {
@@ -1481,7 +1573,20 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
         if (Qf > 0) {
             uint64_t target = (uint64_t)floor((double)p.u * (double)Qf);
             if (target >= Qf) target = Qf - 1;
-            if (target < AC && nC > 0) {
+            if (target < AC && nC > 0 && sorted) {
+                // kept entries within the cut form a prefix of the sorted buffer
+                uint32_t lim = nk;
+                if (cut && !cut_in_R) {
+                    lim = 0u;
+                    for (uint32_t i = tid; i < nk; i += NCT) if (s.ckey[i] >= tstar) lim = max(lim, i + 1u);
+                    lim = cons_max_u32(lim, s, tid);
+                    // only the first m_t entries of the tie run at tstar are kept
+                    lim = (uint32_t)((uint64_t)lim - n_t + m_t);
+                }
+                uint64_t incl = 0;
+                const uint32_t id = sorted_crossing(P, tid, lim, target, My, scale, &incl);
+                if (id < lim) out_id = s.cid[id];
+            } else if (target < AC && nC > 0) {
                 const SelOut sd = block_select<true, false>(
                     [&](auto&& f) {
                         for (uint32_t i0 = 0; i0 < nC; i0 += NCT) {
