@@ -26,8 +26,8 @@ FG_ROW_ERROR_MASK = 0x00FF
 FG_ROW_GENERAL_PATH = 0x0100
 FG_ROW_GREEDY = 0x0200
 
-EXPORTED_SYMBOLS = ("fg_sample", "fg_sample_candidates", "fg_sample_noalloc", "fg_apply_repetition_penalty",
-                    "fg_argmax", "fg_strerror", "fg_version")
+EXPORTED_SYMBOLS = ("fg_sample", "fg_sample_candidates", "fg_sample_noalloc", "fg_sample_set_split",
+                    "fg_apply_repetition_penalty", "fg_argmax", "fg_strerror", "fg_version")
 
 
 class FgSampleArgs(ctypes.Structure):
@@ -59,7 +59,7 @@ class FgSampleArgs(ctypes.Structure):
     ]
 
 
-FG_SAMPLE_WORKSPACE_BYTES = 256
+FG_SAMPLE_WORKSPACE_BYTES = 262144
 
 
 _lib = None
@@ -91,6 +91,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.fg_sample_candidates.restype = ctypes.c_int
         lib.fg_sample_noalloc.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p]
         lib.fg_sample_noalloc.restype = ctypes.c_int
+        lib.fg_sample_set_split.argtypes = [ctypes.c_int]
+        lib.fg_sample_set_split.restype = ctypes.c_int
         lib.fg_apply_repetition_penalty.argtypes = [
             ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]

@@ -90,9 +90,143 @@ const char* fg_strerror(int code) {
 }  // extern "C"
 
 namespace {
+// Shared-memory layout for P (vocab, pen_possible, hu_cap set), then the
+// launch. mass_vocab: how many elements a row's total mass may sum (the merge
+// of the split path sums a whole row's mass over a shorter union row).
+int layout_and_launch(fg::KParams& P, int dtype, DevInfo* d, cudaStream_t st, int64_t mass_vocab = 0) {
+    P.id_bits = bits_for(std::max<int64_t>(P.vocab, mass_vocab));
+    P.mass_shift = 62 - P.id_bits;
+    // two CTAs per SM when one fits in half of the SM's shared memory (with at
+    // least four 8 KB stages); otherwise one CTA per SM with a deeper ring
+    int chosen = 0, smem = 0, per_sm = 1;
+    for (int pass = 0; pass < 2 && chosen == 0; ++pass) {
+        const int limit = pass == 0 ? (d->smem_per_sm / 2 - 1024) : d->smem_optin;
+        const int min_ns = pass == 0 ? 4 : 2;
+        for (int ns = 12; ns >= min_ns; --ns) {
+            int off = fg::head_bytes(ns);
+            const int ob = off; off += 2 * 8 * fg::NB;
+            const int oc = off; off += 2 * 4 * fg::NB;
+            off = fg::align_up_i(off, 16);
+            const int ok = off; off += 4 * fg::CAND_CAP;
+            const int oi = off; off += 4 * fg::CAND_CAP;
+            int obm = 0, opf = 0, ocn = 0, osv = 0, osc = 0;
+            if (P.pen_possible) {
+                off = fg::align_up_i(off, 16); obm = off; off += 4 * P.nwords;
+                off = fg::align_up_i(off, 16); opf = off; off += 2 * ((P.nwords + 1) / 2);
+                off = fg::align_up_i(off, 16); ocn = off; off += 4 * P.hu_cap;
+                off = fg::align_up_i(off, 16); osv = off; off += 4 * P.hu_cap;
+                off = fg::align_up_i(off, 16); osc = off; off += 4 * P.hu_cap;
+            }
+            off = fg::align_up_i(off, 128);
+            const int total = off + ns * fg::TILE_BYTES;
+            if (total <= limit) {
+                chosen = ns; smem = total; per_sm = pass == 0 ? 2 : 1;
+                P.off_bins = ob; P.off_cnts = oc; P.off_ckey = ok; P.off_cid = oi;
+                P.off_bitmap = obm; P.off_prefix = opf; P.off_counts = ocn; P.off_sval = osv; P.off_scol = osc;
+                P.off_ring = off;
+                break;
+            }
+        }
+    }
+    if (chosen == 0) return FG_ENOTSUP;
+    P.nstage = chosen;
+    P.off_ctl = fg::ctl_offset(chosen);
+    const int grid = std::min(P.batch, d->sms * per_sm);
+    switch (dtype) {
+        case FG_DTYPE_F32: return launch_sample<FG_DTYPE_F32>(P, smem, grid, st, d);
+        case FG_DTYPE_F16: return launch_sample<FG_DTYPE_F16>(P, smem, grid, st, d);
+        default: return launch_sample<FG_DTYPE_BF16>(P, smem, grid, st, d);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Split path for small batches. One CTA streaming a whole row is bound by its
+// own per-tile latency, so a batch that leaves most SMs idle has each row cut
+// into G column shards, sampled by G CTAs in three launches on the stream:
+//   1. shard stage: every shard's candidates after penalties and temperature
+//      (its top-k set, or its top kSplitCand values with the key from which
+//      that set is complete) and its mass partial (max, sum of exp);
+//   2. merge: each row's G candidate sets, in column order, sampled as one row
+//      (temperature 1, no penalties) with the whole row's mass; a row whose
+//      cut or draw falls where the union may be incomplete is marked;
+//   3. fixup: the marked rows (and rows with errors) sampled whole.
+// Scratch lives in the workspace after its counters.
+// ---------------------------------------------------------------------------
+constexpr int kSplitCand = 256;        // candidates per shard (<= 2 * NB)
+constexpr int kSplitMinCols = 4096;    // shard width below which splitting does not pay
+constexpr size_t kSplitScratch0 = 4096;
+int g_split_mode = 1;                  // 0 off, 1 automatic, 2 whenever the shapes allow
+
+size_t split_bytes(int64_t B, int G) {
+    const int64_t n = B * G;
+    return kSplitScratch0 + (size_t)n * (8 * kSplitCand + 4 + 4 + 4 + 8 + 16) + (size_t)B * 4 + 16 * 8;
+}
+
+int split_shards(const FgSampleArgs* a, int64_t vtot, const DevInfo* d) {
+    if (g_split_mode == 0 || a->out_probs != nullptr) return 0;
+    if (a->vocab_offset != 0 || vtot != a->vocab) return 0;
+    if (a->batch > 1 && a->row_stride != a->vocab) return 0;
+    for (int G = 32; G >= 4; G >>= 1) {
+        if (a->vocab % G != 0) continue;
+        const int W = a->vocab / G;
+        if (W < 32) continue;
+        if (g_split_mode == 1 && (W < kSplitMinCols || (int64_t)a->batch * G > d->sms)) continue;
+        if (split_bytes(a->batch, G) > (size_t)FG_SAMPLE_WORKSPACE_BYTES) continue;
+        return G;
+    }
+    return 0;
+}
+
+int split_launch(const fg::KParams& P0, const FgSampleArgs* a, int G, DevInfo* d, cudaStream_t st) {
+    const int64_t B = a->batch, n = B * G;
+    uint8_t* w = reinterpret_cast<uint8_t*>(a->workspace) + kSplitScratch0;
+    auto take = [&](size_t bytes) { uint8_t* p = w; w += (bytes + 15) & ~size_t(15); return p; };
+    float* cvals = reinterpret_cast<float*>(take(sizeof(float) * n * kSplitCand));
+    int32_t* cids = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * n * kSplitCand));
+    int32_t* ccount = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * n));
+    uint32_t* cthr = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * n));
+    int32_t* cstat = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * n));
+    int64_t* cout = reinterpret_cast<int64_t*>(take(sizeof(int64_t) * n));
+    double* cmz = reinterpret_cast<double*>(take(sizeof(double) * 2 * n));
+    int32_t* mstat = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * B));
+
+    // 1. shard stage: launch row r is row r / G, columns [(r % G) * W, ... + W)
+    fg::KParams S = P0;
+    S.batch = (int32_t)n;
+    S.vocab = a->vocab / G;
+    S.row_stride = S.vocab;
+    S.nshard = G;
+    S.cand_vals = cvals; S.cand_ids = cids; S.cand_count = ccount; S.cand_max = kSplitCand;
+    S.cand_thr = cthr; S.cand_mz = cmz;
+    S.out_ids = cout; S.out_status = cstat; S.out_probs = nullptr;
+    S.nwords = (S.vocab + 31) / 32;
+    if (S.pen_possible) S.hu_cap = std::max(1, std::min(a->hist_max_len, S.vocab));
+    int rc = layout_and_launch(S, a->dtype, d, st);
+    if (rc != FG_OK) return rc;
+
+    // 2. merge: row r is the union of its G shard sets (fp32 values)
+    fg::KParams M = P0;
+    M.logits = cvals; M.vocab = G * kSplitCand; M.row_stride = M.vocab;
+    M.vocab_offset = 0; M.vocab_total = M.vocab;
+    M.hist_ids = nullptr; M.hist_offsets = nullptr;
+    M.rep = nullptr; M.pres = nullptr; M.freq = nullptr;
+    M.pen_possible = 0; M.hu_cap = 0;
+    M.nwords = (M.vocab + 31) / 32;
+    M.merge_g = G; M.id_map = cids; M.shard_mz = cmz; M.shard_thr = cthr; M.shard_status = cstat;
+    M.out_status = mstat; M.final_status = a->out_status; M.out_probs = nullptr;
+    rc = layout_and_launch(M, FG_DTYPE_F32, d, st, a->vocab);
+    if (rc != FG_OK) return rc;
+
+    // 3. fixup: the rows the merge left undecided, sampled whole
+    fg::KParams F = P0;
+    F.redo = mstat;
+    return layout_and_launch(F, a->dtype, d, st);
+}
+
 // fg_sample's launch; the candidate outputs are non-null only for
 // fg_sample_candidates.
-int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* cids, int32_t* ccount, int32_t cmax) {
+int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* cids, int32_t* ccount, int32_t cmax,
+                  bool allow_split) {
     if (a == nullptr) return FG_EINVAL;
     const int esz = elem_size(a->dtype);
     if (esz == 0 || a->logits == nullptr || a->batch < 0 || a->vocab < 1) return FG_EINVAL;
@@ -131,64 +265,29 @@ int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* ci
     } else {
         P.hu_cap = 0;
     }
-    P.id_bits = bits_for(a->vocab);
-    P.mass_shift = 62 - P.id_bits;
-
-    // two CTAs per SM when one fits in half of the SM's shared memory (with at
-    // least four 8 KB stages); otherwise one CTA per SM with a deeper ring
-    int chosen = 0, smem = 0, per_sm = 1;
-    for (int pass = 0; pass < 2 && chosen == 0; ++pass) {
-        const int limit = pass == 0 ? (d->smem_per_sm / 2 - 1024) : d->smem_optin;
-        const int min_ns = pass == 0 ? 4 : 2;
-        for (int ns = 12; ns >= min_ns; --ns) {
-            int off = fg::head_bytes(ns);
-            const int ob = off; off += 2 * 8 * fg::NB;
-            const int oc = off; off += 2 * 4 * fg::NB;
-            off = fg::align_up_i(off, 16);
-            const int ok = off; off += 4 * fg::CAND_CAP;
-            const int oi = off; off += 4 * fg::CAND_CAP;
-            int obm = 0, opf = 0, ocn = 0, osv = 0, osc = 0;
-            if (P.pen_possible) {
-                off = fg::align_up_i(off, 16); obm = off; off += 4 * P.nwords;
-                off = fg::align_up_i(off, 16); opf = off; off += 2 * ((P.nwords + 1) / 2);
-                off = fg::align_up_i(off, 16); ocn = off; off += 4 * P.hu_cap;
-                off = fg::align_up_i(off, 16); osv = off; off += 4 * P.hu_cap;
-                off = fg::align_up_i(off, 16); osc = off; off += 4 * P.hu_cap;
-            }
-            off = fg::align_up_i(off, 128);
-            const int total = off + ns * fg::TILE_BYTES;
-            if (total <= limit) {
-                chosen = ns; smem = total; per_sm = pass == 0 ? 2 : 1;
-                P.off_bins = ob; P.off_cnts = oc; P.off_ckey = ok; P.off_cid = oi;
-                P.off_bitmap = obm; P.off_prefix = opf; P.off_counts = ocn; P.off_sval = osv; P.off_scol = osc;
-                P.off_ring = off;
-                break;
-            }
-        }
-    }
-    if (chosen == 0) return FG_ENOTSUP;
-    P.nstage = chosen;
-    P.off_ctl = fg::ctl_offset(chosen);
-    const int grid = std::min(a->batch, d->sms * per_sm);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    switch (a->dtype) {
-        case FG_DTYPE_F32: return launch_sample<FG_DTYPE_F32>(P, smem, grid, st, d);
-        case FG_DTYPE_F16: return launch_sample<FG_DTYPE_F16>(P, smem, grid, st, d);
-        default: return launch_sample<FG_DTYPE_BF16>(P, smem, grid, st, d);
-    }
+    const int G = (cvals == nullptr && allow_split) ? split_shards(a, vtot, d) : 0;
+    if (G > 1) return split_launch(P, a, G, d, st);
+    return layout_and_launch(P, a->dtype, d, st);
 }
 }  // namespace
 
 extern "C" {
 
 int fg_sample(const FgSampleArgs* a, void* stream) {
-    return sample_launch(a, stream, nullptr, nullptr, nullptr, 0);
+    return sample_launch(a, stream, nullptr, nullptr, nullptr, 0, true);
+}
+
+int fg_sample_set_split(int mode) {
+    if (mode < 0 || mode > 2) return FG_EINVAL;
+    g_split_mode = mode;
+    return FG_OK;
 }
 
 int fg_sample_candidates(const FgSampleArgs* a, float* vals, int32_t* gids, int32_t* counts, int32_t cand_max,
                          void* stream) {
     if (vals == nullptr || gids == nullptr || counts == nullptr || cand_max < 1) return FG_EINVAL;
-    return sample_launch(a, stream, vals, gids, counts, cand_max);
+    return sample_launch(a, stream, vals, gids, counts, cand_max, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -208,7 +307,7 @@ constexpr size_t kNoAllocScratchBytes = 256;
 constexpr int32_t kNoAllocMaxBatch = 1 << 30;   // the queue counter runs to about 2 * batch in 32 bits
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 void* g_noalloc_ptr[kMaxDevices] = {};
-static_assert(FG_SAMPLE_WORKSPACE_BYTES <= kNoAllocScratchBytes, "static scratch smaller than the workspace");
+static_assert(sizeof(fg::Workspace) <= kNoAllocScratchBytes, "static scratch smaller than the row-queue counters");
 }  // namespace
 
 int fg_sample_noalloc(const FgSampleArgs* a, void* stream) {
@@ -230,7 +329,8 @@ int fg_sample_noalloc(const FgSampleArgs* a, void* stream) {
     }
     FgSampleArgs b = *a;
     b.workspace = ws;
-    return fg_sample(&b, stream);
+    // the fixed scratch holds the row-queue counters only: no split path
+    return sample_launch(&b, stream, nullptr, nullptr, nullptr, 0, false);
 }
 
 int fg_argmax(const void* logits, int32_t dtype, int32_t batch, int32_t vocab, int64_t row_stride,

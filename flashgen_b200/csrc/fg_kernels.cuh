@@ -195,7 +195,9 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
     const int lane = tid & 31;
     for (int w = tid; w < nw; w += NCT) s.bitmap[w] = 0u;
     csync();
-    const int64_t h0 = __ldg(P.hist_offsets + r), h1 = __ldg(P.hist_offsets + r + 1);
+    const int q = src_row(P, r);
+    const int64_t h0 = __ldg(P.hist_offsets + q), h1 = __ldg(P.hist_offsets + q + 1);
+    const int64_t cb = col_base(P, r);
     constexpr int HB = 4;        // ids per thread per batch, loaded together
     constexpr int HOWN = 4 * HB; // first-setters remembered in registers (histories <= NCT * HOWN)
     int bad = 0;
@@ -217,7 +219,7 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
             if (i >= h1) continue;
             const int64_t gid = ids[j];
             if (gid < 0 || gid >= P.vocab_total) { bad = 1; continue; }
-            const int64_t c = gid - P.vocab_offset;
+            const int64_t c = gid - cb;
             if (c >= 0 && c < P.vocab) {
                 const uint32_t bit = 1u << (c & 31);
                 if (!(s.bitmap[c >> 5] & bit)) {
@@ -309,7 +311,7 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
             for (int j = 0; j < HB; ++j) {
                 const int64_t i = b0 + tid + (int64_t)j * NCT;
                 const int64_t gid = ids[j];
-                const int64_t c = gid - P.vocab_offset;
+                const int64_t c = gid - cb;
                 bool v = i < h1 && gid >= 0 && gid < P.vocab_total && c >= 0 && c < P.vocab;
                 const uint32_t rk = v ? hist_rank(s, (uint32_t)c) : 0u;
                 v = v && rk < U;
@@ -1179,7 +1181,8 @@ __device__ void producer(const KParams& P, const Smem& s) {
 #pragma unroll
             for (int i = 0; i < ROW_CLAIM; ++i) {
                 const unsigned u = v + (unsigned)i;
-                if (u < 2u * B && (u < B) == hv[i]) held[nheld++] = (int)(u % B) | (hv[i] ? HEAVY : 0);
+                if (u < 2u * B && (u < B) == hv[i] && row_wanted(P, (int)(u % B)))
+                    held[nheld++] = (int)(u % B) | (hv[i] ? HEAVY : 0);
             }
         }
         return held[hpos++];
@@ -1362,7 +1365,27 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
         Zq = Zd * exp((double)M / (double)p.T - (double)My) * (double)scale;
         ymin = ydiv(p, cons_min_f(st.tmin, s, tid));
     }
+    // merge stage of the split path: the row's total mass from the shards'
+    // partials (the union holds only their candidates), the key from which
+    // the union is complete, and the shards' status words
+    uint32_t thr_max = 0u;
+    int shard_or = 0;
+    bool split_redo = false;
+    if (P.merge_g > 0) {
+        double zt = 0.0;
+        for (int j = 0; j < P.merge_g; ++j) {
+            const int64_t sj = (int64_t)r * P.merge_g + j;
+            thr_max = max(thr_max, __ldg(P.shard_thr + sj));
+            shard_or |= __ldg(P.shard_status + sj);
+            const double my = __ldg(P.shard_mz + 2 * sj), z = __ldg(P.shard_mz + 2 * sj + 1);
+            if (z > 0.0) zt += z * exp(my - (double)My);
+        }
+        if (p.zsum && Zq > 0.0) Zq = zt * (double)scale;
+        // a shard whose columns are all -inf just has an empty set
+        split_redo = (shard_or & (FG_ROW_ERROR_MASK & ~FG_ROW_ALL_MASKED)) != 0;
+    }
     int64_t out_id = -1;
+    bool cand_written = false;   // candidates mode: this row's set was written
     float* pr = P.out_probs ? P.out_probs + (int64_t)r * P.vocab : nullptr;
 
     if (aborted) {
@@ -1407,9 +1430,17 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
             const bool any = best != 0xffffffffu;
             for (int i = tid; i < P.cand_max; i += NCT) {
                 cv[i] = (i == 0 && any) ? M : -INFINITY;
-                cg[i] = (i == 0 && any) ? (int32_t)(best + P.vocab_offset) : INT32_MAX;
+                cg[i] = (i == 0 && any) ? (int32_t)(best + col_base(P, r)) : INT32_MAX;
             }
-            if (tid == 0) P.cand_count[r] = any ? 1 : 0;
+            if (tid == 0) {
+                P.cand_count[r] = any ? 1 : 0;
+                if (P.cand_mz != nullptr) {
+                    P.cand_thr[r] = 0xffffffffu;
+                    P.cand_mz[2 * (int64_t)r] = 0.0;
+                    P.cand_mz[2 * (int64_t)r + 1] = 0.0;
+                }
+            }
+            cand_written = true;
         }
         if (pr) for (int c = tid; c < P.vocab; c += NCT) pr[c] = (c == (int)best) ? 1.0f : 0.0f;
     } else if (M != M) {
@@ -1464,7 +1495,62 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
             }
         }
         auto keepk = [&](uint32_t yk) { return p.mode != MODE_TOPK || yk >= ykK; };
-        if (P.cand_vals != nullptr) {
+        if (P.cand_vals != nullptr && P.cand_mz != nullptr) {
+            // shard stage of the split path: the shard's top-k set (top-k
+            // rows) or its top cand_max values (other rows), in column order,
+            // with the key from which the output is complete and the shard's
+            // mass partial
+            uint32_t klo_out = 0u, thr = 0u;
+            bool trunc = !cand_ok;
+            if (cand_ok && p.mode == MODE_TOPK) {
+                klo_out = ykK; thr = ykK;
+            } else if (cand_ok && nC > (uint32_t)P.cand_max) {
+                const SelOut so = block_select<true, true>(
+                    [&](auto&& f) {
+                        for (uint32_t i0 = 0; i0 < nC; i0 += NCT) {
+                            const uint32_t i = i0 + tid;
+                            f(i < nC, i < nC ? s.ckey[i] : 0u, 1ull);
+                        }
+                    },
+                    (uint64_t)(P.cand_max - 1), cLo, remC, s, tid);
+                if (!so.ok || so.key == 0xffffffffu) trunc = true;
+                klo_out = so.key + 1u; thr = klo_out;
+            } else if (cand_ok) {
+                klo_out = 0u; thr = loY;
+            }
+            if (tid == 0) ctl->ncol = 0u;
+            csync();
+            if (!trunc) {
+                for (uint32_t i = tid; i < nC; i += NCT) {
+                    if (s.ckey[i] < klo_out) continue;
+                    const uint32_t pos = atoms_add(&ctl->ncol, 1u);
+                    if (pos < (uint32_t)P.cand_max) { s.blo[pos] = s.ckey[i]; s.bhi[pos] = s.cid[i]; }
+                }
+            }
+            csync();
+            const uint32_t cnt = ctl->ncol;
+            if (trunc || cnt > (uint32_t)P.cand_max) status |= FG_ROW_CAND_TRUNC;
+            const uint32_t w = min(cnt, (uint32_t)P.cand_max);
+            float* cv = P.cand_vals + (int64_t)r * P.cand_max;
+            int32_t* cg = P.cand_ids + (int64_t)r * P.cand_max;
+            const int64_t cb = col_base(P, r);
+            // position = rank by column among the output (columns are distinct)
+            for (uint32_t i = tid; i < w; i += NCT) {
+                const uint32_t ci = s.bhi[i];
+                uint32_t rank = 0;
+                for (uint32_t j = 0; j < w; ++j) rank += s.bhi[j] < ci ? 1u : 0u;
+                cv[rank] = funkey(s.blo[i]);
+                cg[rank] = (int32_t)(ci + cb);
+            }
+            for (uint32_t i = w + tid; i < (uint32_t)P.cand_max; i += NCT) { cv[i] = -INFINITY; cg[i] = INT32_MAX; }
+            cand_written = true;
+            if (tid == 0) {
+                P.cand_count[r] = (int32_t)w;
+                P.cand_thr[r] = thr;
+                P.cand_mz[2 * (int64_t)r] = (double)My;
+                P.cand_mz[2 * (int64_t)r + 1] = Zq / (double)scale;
+            }
+        } else if (P.cand_vals != nullptr) {
             // candidates mode (a vocabulary shard): the row's top-k set, ties
             // included, as (y, global id); the draw happens after the merge
             if (p.mode != MODE_TOPK) {
@@ -1476,7 +1562,7 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
                 int32_t* cg = P.cand_ids + (int64_t)r * P.cand_max;
                 auto put = [&](uint32_t yk, uint32_t col) {
                     const uint32_t pos = atoms_add(&ctl->ncol, 1u);
-                    if (pos < (uint32_t)P.cand_max) { cv[pos] = funkey(yk); cg[pos] = (int32_t)(col + P.vocab_offset); }
+                    if (pos < (uint32_t)P.cand_max) { cv[pos] = funkey(yk); cg[pos] = (int32_t)(col + col_base(P, r)); }
                 };
                 if (nC > 0) {
                     for (uint32_t i = tid; i < nC; i += NCT) if (s.ckey[i] >= ykK) put(s.ckey[i], s.cid[i]);
@@ -1508,6 +1594,7 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
         const float yRhi = nC > 0 ? funkey(loY - 1u) : My;
         bool cut = false, cut_in_R = false;
         uint32_t tstar = 0u, id_cut = 0xffffffffu;
+        uint32_t dkey = 0u;   // y-key of the drawn element when drawn from C
         uint64_t Qf = 0, m_t = 0, n_t = 0;
         if (p.use_p) {
             double Qn;
@@ -1585,7 +1672,7 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
                 }
                 uint64_t incl = 0;
                 const uint32_t id = sorted_crossing(P, tid, lim, target, My, scale, &incl);
-                if (id < lim) out_id = s.cid[id];
+                if (id < lim) { out_id = s.cid[id]; dkey = s.ckey[id]; }
             } else if (target < AC && nC > 0) {
                 const SelOut sd = block_select<true, false>(
                     [&](auto&& f) {
@@ -1602,6 +1689,7 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
                     uint64_t j = qd ? (target - sd.before) / qd : 0;
                     if (j >= sd.n_at) j = sd.n_at ? sd.n_at - 1 : 0;
                     out_id = jth_id(P, s, tid, 0u, nC, sd.key, sd.n_at, j);
+                    dkey = sd.key;
                 }
             } else {
                 status |= FG_ROW_GENERAL_PATH;
@@ -1617,6 +1705,12 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
                                          : jth_id_row<DT>(P, s, p, r, g, tid, L.key, j);
                 }
             }
+        }
+        // merge stage: exact only when the decision lies in the union's
+        // complete part and inside the merge's candidate set
+        if (P.merge_g > 0 && p.mode != MODE_TOPK) {
+            if ((status & FG_ROW_GENERAL_PATH) || (cut && !cut_in_R && tstar < thr_max) || dkey < thr_max)
+                split_redo = true;
         }
         if (out_id < 0 && !(status & FG_ROW_ERROR_MASK)) status |= FG_ROW_ALL_MASKED;
         // ---- kept-set probabilities (debug / oracle mode) ----
@@ -1662,9 +1756,32 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
         }   // end of the sampling decision (not run in candidates mode)
     }
     if (pr && out_id < 0) for (int c = tid; c < P.vocab; c += NCT) pr[c] = 0.0f;
+    if (P.cand_mz != nullptr && !cand_written) {
+        // shard stage, no set written above (a row error): an empty set,
+        // complete when the shard's columns are all -inf
+        float* cv = P.cand_vals + (int64_t)r * P.cand_max;
+        int32_t* cg = P.cand_ids + (int64_t)r * P.cand_max;
+        for (int i = tid; i < P.cand_max; i += NCT) { cv[i] = -INFINITY; cg[i] = INT32_MAX; }
+        if (tid == 0) {
+            P.cand_count[r] = 0;
+            P.cand_thr[r] = (status & FG_ROW_ERROR_MASK) == FG_ROW_ALL_MASKED ? 0u : 0xffffffffu;
+            P.cand_mz[2 * (int64_t)r] = 0.0;
+            P.cand_mz[2 * (int64_t)r + 1] = 0.0;
+        }
+    }
     if (tid == 0) {
-        P.out_ids[r] = (out_id >= 0) ? out_id + P.vocab_offset : -1;
-        if (P.out_status) P.out_status[r] = status;
+        if (P.merge_g > 0) {
+            // an error of the union itself (say, every shard's set empty after
+            // a run of ties) is not the row's: the row is sampled whole
+            if (status & FG_ROW_ERROR_MASK) split_redo = true;
+            if (split_redo) { status |= FG_ROW_SPLIT_REDO; out_id = -1; }
+            P.out_ids[r] = (out_id >= 0) ? (int64_t)__ldg(P.id_map + (int64_t)r * P.vocab + out_id) : -1;
+            if (P.out_status) P.out_status[r] = status;
+            if (P.final_status && !split_redo) P.final_status[r] = status;
+        } else {
+            P.out_ids[r] = (out_id >= 0) ? out_id + col_base(P, r) : -1;
+            if (P.out_status) P.out_status[r] = status;
+        }
     }
     csync();
     if (aborted && tid == 0) *abort = 1;
@@ -2094,6 +2211,7 @@ __device__ void consumer(const KParams& P, const int tid) {
             const unsigned v = atomicAdd(&P.ws->next_row, 1u);
             if (v >= 2u * (unsigned)P.batch) break;
             if (!row_owned(P, v)) continue;   // handed out in the other half of the queue
+            if (!row_wanted(P, (int)(v % (unsigned)P.batch))) continue;
             const unsigned rr = v % (unsigned)P.batch;
             P.out_ids[rr] = -1;
             if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT;

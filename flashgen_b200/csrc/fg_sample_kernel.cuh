@@ -81,7 +81,29 @@ struct KParams {
     int32_t pen_possible;
     int32_t mass_shift;      // S: masses are round(e * 2^S)
     int32_t id_bits;         // bits needed for a column index
+    // ---- split path for small batches: each row's columns are cut into
+    //      nshard shards sampled by different CTAs, whose candidates are merged
+    // shard stage (nshard > 1): launch row r is shard r % nshard of row
+    // r / nshard, columns [(r % nshard) * vocab, ... + vocab); candidates mode
+    // with the outputs below, sorted by column
+    int32_t nshard;
+    double* cand_mz;           // [rows][2]: y maximum and sum of exp(y - that maximum)
+    uint32_t* cand_thr;        // [rows]: y-key from which the row's output is complete
+    // merge stage (merge_g > 0): launch row r is the union of row r's
+    // merge_g shard outputs, already penalised and divided by T
+    int32_t merge_g;
+    const int32_t* id_map;     // [rows][vocab] global id of each union column
+    const double* shard_mz;    // [rows * merge_g][2]
+    const uint32_t* shard_thr; // [rows * merge_g]
+    const int32_t* shard_status;
+    int32_t* final_status;     // the caller's status array (rows finished here)
+    // fixup stage (redo != null): only rows whose redo word has FG_ROW_SPLIT_REDO
+    const int32_t* redo;
 };
+
+// Internal row status bit of the split path: the merge could not decide the
+// row exactly from the shards' candidates; the fixup stage samples it whole.
+constexpr int FG_ROW_SPLIT_REDO = 0x4000;
 
 struct SelSlot {
     int ok;
@@ -232,18 +254,28 @@ struct RowParams {
     int bad;         // FG_ROW_BAD_PARAM / FG_ROW_BAD_UNIFORM
 };
 
+// Split path: the caller's row of launch row r, and the global id of the
+// launch row's column 0.
+__device__ __forceinline__ int src_row(const KParams& P, int r) { return P.nshard > 1 ? r / P.nshard : r; }
+__device__ __forceinline__ int64_t col_base(const KParams& P, int r) {
+    return P.vocab_offset + (P.nshard > 1 ? (int64_t)(r % P.nshard) * P.vocab : 0);
+}
+
 __device__ __forceinline__ RowParams row_params(const KParams& P, int r) {
     RowParams p;
-    p.T = __ldg(P.temperature + r);
-    p.top_p = __ldg(P.top_p + r);
-    const int tk = __ldg(P.top_k + r);
-    p.rep = P.rep ? __ldg(P.rep + r) : 1.0f;
-    p.pres = P.pres ? __ldg(P.pres + r) : 0.0f;
-    p.freq = P.freq ? __ldg(P.freq + r) : 0.0f;
-    const bool g = P.greedy ? (__ldg(P.greedy + r) != 0) : false;
-    p.u = __ldg(P.uniforms + r);
+    const int q = src_row(P, r);
+    p.T = __ldg(P.temperature + q);
+    p.top_p = __ldg(P.top_p + q);
+    const int tk = __ldg(P.top_k + q);
+    p.rep = P.rep ? __ldg(P.rep + q) : 1.0f;
+    p.pres = P.pres ? __ldg(P.pres + q) : 0.0f;
+    p.freq = P.freq ? __ldg(P.freq + q) : 0.0f;
+    const bool g = P.greedy ? (__ldg(P.greedy + q) != 0) : false;
+    p.u = __ldg(P.uniforms + q);
     p.bad = 0;
-    const bool hist = P.pen_possible && (__ldg(P.hist_offsets + r + 1) > __ldg(P.hist_offsets + r));
+    // the merge samples values already divided by T
+    if (P.merge_g > 0 && !g && p.T > 0.0f) p.T = 1.0f;
+    const bool hist = P.pen_possible && (__ldg(P.hist_offsets + q + 1) > __ldg(P.hist_offsets + q));
     p.rep_on = hist && (p.rep != 1.0f);
     p.freq_on = hist && (p.freq != 0.0f);
     p.pres_on = hist && (p.pres != 0.0f);
@@ -267,7 +299,9 @@ __device__ __forceinline__ RowParams row_params(const KParams& P, int r) {
         p.cand = (p.K <= K_FAST_MAX);
     } else {
         p.mode = p.use_p ? MODE_NUCLEUS : MODE_FULL;
-        p.K = K_NUCLEUS; p.cand = true; p.zsum = true;
+        // a shard of the split path keeps at most cand_max candidates
+        p.K = (P.nshard > 1 && P.cand_max < K_NUCLEUS) ? P.cand_max : K_NUCLEUS;
+        p.cand = true; p.zsum = true;
     }
     return p;
 }
@@ -280,11 +314,16 @@ __device__ __forceinline__ RowParams row_params(const KParams& P, int r) {
 // CTA two long rows to run back to back while other CTAs have none.
 constexpr int ROW_CLAIM = 1;
 __device__ __forceinline__ bool row_heavy(const KParams& P, int r) {
-    const float T = __ldg(P.temperature + r);
-    const bool g = P.greedy ? (__ldg(P.greedy + r) != 0) : false;
-    const int tk = __ldg(P.top_k + r);
+    const int q = src_row(P, r);
+    const float T = __ldg(P.temperature + q);
+    const bool g = P.greedy ? (__ldg(P.greedy + q) != 0) : false;
+    const int tk = __ldg(P.top_k + q);
     if (g || T == 0.0f) return false;
     return tk <= 0 || tk > K_FAST_MAX;
+}
+// Fixup stage of the split path: only the rows the merge could not decide.
+__device__ __forceinline__ bool row_wanted(const KParams& P, int r) {
+    return P.redo == nullptr || (__ldg(P.redo + r) & FG_ROW_SPLIT_REDO) != 0;
 }
 __device__ __forceinline__ bool row_owned(const KParams& P, unsigned v) {
     const unsigned B = (unsigned)P.batch;

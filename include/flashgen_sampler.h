@@ -128,12 +128,15 @@ typedef struct FgSampleArgs {
 } FgSampleArgs;
 
 /*
- * Workspace: rows are handed to the GPU's persistent CTAs through a counter in
- * this small device buffer. The caller zeroes it once (cudaMemset) before its
- * first use; every fg_sample call leaves it zeroed again. Calls that may run
- * concurrently on the GPU (different streams) need separate workspaces.
+ * Workspace: rows are handed to the GPU's persistent CTAs through counters in
+ * the first 256 bytes of this device buffer. The caller zeroes the buffer once
+ * (cudaMemset) before its first use; every fg_sample call leaves the counters
+ * zero again. The rest is scratch for small batches, whose rows fg_sample cuts
+ * into column shards sampled by several CTAs (see fg_sample_set_split). Calls
+ * that may run concurrently on the GPU (different streams) need separate
+ * workspaces.
  */
-#define FG_SAMPLE_WORKSPACE_BYTES 256
+#define FG_SAMPLE_WORKSPACE_BYTES 262144
 
 /*
  * Batched fused sampling (one decode step). Replaces Sampler.sample
@@ -162,6 +165,25 @@ int fg_sample(const FgSampleArgs* args, void* stream);
  */
 int fg_sample_candidates(const FgSampleArgs* args, float* vals, int32_t* gids,
                          int32_t* counts, int32_t cand_max, void* stream);
+
+/*
+ * Small-batch split path of fg_sample (no reference counterpart; FlashGen
+ * samples one row per call on the CPU). When a batch leaves most SMs idle,
+ * each row's columns are cut into G shards (G a power of two dividing vocab)
+ * sampled by G CTAs: per shard the candidates after penalties and temperature
+ * and a mass partial, then one merge per row that draws from the union with
+ * the whole row's mass, then a fixup launch that samples whole any row the
+ * union could not decide exactly (a cut or draw below the union's complete
+ * part, a shard error). The kept set and the draw order are the unsplit
+ * path's; integer masses are rounded at another scale and the row total is
+ * summed in another order, so a draw may differ only where the uniform lies
+ * within rounding of a CDF boundary (the parity tolerance). mode 0 turns it
+ * off, 1 (default) uses it when B * G <= SMs and vocab / G >= 4096, 2 uses it
+ * whenever the shapes allow (tests). Process-wide; returns FG_EINVAL for other
+ * modes. Not used by fg_sample_candidates or fg_sample_noalloc, nor with
+ * out_probs, vocab shards (vocab_offset, vocab_total) or padded rows.
+ */
+int fg_sample_set_split(int mode);
 
 /*
  * fg_sample without a caller workspace: args->workspace must be NULL, and the

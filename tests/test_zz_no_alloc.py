@@ -58,4 +58,4 @@ def test_noalloc_matches_fg_sample(cuda_device, cfg, batch):
         assert (st_b.cpu().numpy() & _lib.FG_ROW_ERROR_MASK == 0).all(), call
         np.testing.assert_array_equal(out_b.cpu().numpy(), out_a.cpu().numpy())
         np.testing.assert_array_equal(st_b.cpu().numpy(), st_a.cpu().numpy())
-    assert (ws.cpu().numpy() == 0).all()
+    assert (ws[:64].cpu().numpy() == 0).all()   # the row-queue counters
