@@ -206,12 +206,21 @@ __device__ void history_prologue(const KParams& P, const Smem& s, const RowParam
     uint32_t own_col[HOWN];
     uint32_t owned = 0u;
     int bi = 0;
+    // the next batch's ids are loaded before this batch's bitmap atomics, so
+    // one global-load latency is paid per history rather than per batch
+    int32_t nxt[HB];
+#pragma unroll
+    for (int j = 0; j < HB; ++j) {
+        const int64_t i = h0 + tid + (int64_t)j * NCT;
+        nxt[j] = i < h1 ? __ldg(P.hist_ids + i) : -1;
+    }
     for (int64_t b0 = h0; b0 < h1; b0 += (int64_t)NCT * HB, ++bi) {
         int32_t ids[HB];
 #pragma unroll
         for (int j = 0; j < HB; ++j) {
-            const int64_t i = b0 + tid + (int64_t)j * NCT;
-            ids[j] = i < h1 ? __ldg(P.hist_ids + i) : -1;
+            ids[j] = nxt[j];
+            const int64_t i = b0 + (int64_t)NCT * HB + tid + (int64_t)j * NCT;
+            nxt[j] = i < h1 ? __ldg(P.hist_ids + i) : -1;
         }
 #pragma unroll
         for (int j = 0; j < HB; ++j) {
@@ -913,6 +922,90 @@ struct WLoc {
     Located L;
 };
 
+// The passes of the windowed locate, each its own function with scalar
+// arguments: the per-element loop then keeps its few values in registers
+// instead of reloading the caller's spilled state for every element.
+template <int DT>
+__device__ __noinline__ void wpass_count(const KParams& P, int tid, int r, float a0, float bi, float xlo, float xhi) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    uint32_t* cnt = s.blo;
+    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+        if (valid && x >= a0 && x <= xhi && x >= xlo) reds_add(&cnt[wbin(x, a0, bi)], 1u);
+    });
+}
+// Mass above the window (per thread), counts inside it. Branch-free per
+// element: the mass is computed for every element and added under a
+// predicate, so a warp does not run both paths.
+template <int DT>
+__device__ __noinline__ uint64_t wpass_mass(const KParams& P, int tid, int r, float a0, float a1, float bi, float xlo,
+                                            float xhi, float cxx, float nmy, float scale) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    uint32_t* cnt = s.blo;
+    uint64_t acc = 0;
+    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+        const bool inr = valid && x >= xlo && x <= xhi;
+        const uint64_t q = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+        acc += (inr && x > a1) ? q : 0ull;
+        if (inr && x <= a1 && x >= a0) reds_add(&cnt[wbin(x, a0, bi)], 1u);
+    });
+    return acc;
+}
+struct WRun { uint64_t acc, cnt; };
+// Mass above a run of equal values [a0, a1] and its length (per thread).
+template <int DT>
+__device__ __noinline__ WRun wpass_run(const KParams& P, int tid, int r, float a0, float a1, float xlo, float xhi,
+                                       float cxx, float nmy, float scale) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    WRun w{0ull, 0ull};
+    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+        const bool inr = valid && x >= xlo && x <= xhi;
+        const uint64_t q = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+        w.acc += (inr && x > a1) ? q : 0ull;
+        w.cnt += (inr && x <= a1 && x >= a0) ? 1u : 0u;
+    });
+    return w;
+}
+struct WCol { uint64_t acc; uint32_t kmn, kmx; };
+// Collects the window [a0, a1] into the buffer from slot0 (counter
+// ctl->ncol, zero on entry); per thread, the mass above the window and the
+// key range collected.
+template <int DT>
+__device__ __noinline__ WCol wpass_collect(const KParams& P, int tid, int r, float a0, float a1, float xlo, float xhi,
+                                           float cxx, float nmy, float scale, uint32_t slot0) {
+    const Smem s = carve(smem_base(), P);
+    const RowParams p = row_params(P, r);
+    const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
+    const int lane = tid & 31;
+    WCol w{0ull, 0xffffffffu, 0u};
+    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
+        const bool inr = valid && x >= xlo && x <= xhi;
+        const bool in = inr && x >= a0 && x <= a1;
+        const uint64_t qa = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
+        w.acc += (inr && x > a1) ? qa : 0ull;
+        const uint32_t bal = __ballot_sync(0xffffffffu, in);
+        if (bal) {
+            const int lead = __ffs(bal) - 1;
+            uint32_t b0 = 0u;
+            if (lane == lead) b0 = atoms_add(&s.ctl->ncol, (uint32_t)__popc(bal));
+            b0 = __shfl_sync(0xffffffffu, b0, lead);
+            if (in) {
+                const uint32_t k = fkey(ydiv(p, x));
+                const uint32_t pos = slot0 + b0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
+                if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = k; s.cid[pos] = (uint32_t)c; }
+                w.kmn = min(w.kmn, k);
+                w.kmx = max(w.kmx, k);
+            }
+        }
+    });
+    return w;
+}
+
 template <int DT>
 __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g, int tid,
                         uint32_t rlo, uint32_t rhi, float ylo, float yhi, uint64_t target, float My, float scale,
@@ -951,18 +1044,9 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
         const float a0 = wl, a1 = wu, bi = inv;
         if (d == 0) {
             // nothing lies above level 0's range: counts only
-            for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
-                if (valid && x >= a0 && x <= xhi && x >= xlo) reds_add(&cnt[wbin(x, a0, bi)], 1u);
-            });
+            wpass_count<DT>(P, tid, r, a0, bi, xlo, xhi);
         } else {
-            // branch-free per element: the mass is computed for every element
-            // and added under a predicate, so a warp does not run both paths
-            for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
-                const bool inr = valid && x >= xlo && x <= xhi;
-                const uint64_t q = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
-                acc += (inr && x > a1) ? q : 0ull;
-                if (inr && x <= a1 && x >= a0) reds_add(&cnt[wbin(x, a0, bi)], 1u);
-            });
+            acc = wpass_mass<DT>(P, tid, r, a0, a1, bi, xlo, xhi, cxx, nmy, scale);
         }
         csync();
         if (d > 0) above = cons_sum_u64(acc, s, tid);
@@ -993,13 +1077,8 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
         // exact mass above the run and its length; every element of the run
         // has the same y, hence the same mass
         const float a0 = wl, a1 = wu;
-        uint64_t accA = 0, cnt = 0;
-        for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
-            const bool inr = valid && x >= xlo && x <= xhi;
-            const uint64_t q = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
-            accA += (inr && x > a1) ? q : 0ull;
-            cnt += (inr && x <= a1 && x >= a0) ? 1u : 0u;
-        });
+        const WRun wr = wpass_run<DT>(P, tid, r, a0, a1, xlo, xhi, cxx, nmy, scale);
+        const uint64_t accA = wr.acc, cnt = wr.cnt;
         const uint64_t A = cons_sum_u64(accA, s, tid);
         const uint64_t n_at = cons_sum_u64(cnt, s, tid);
         const uint32_t key = fkey(ydiv(p, wl));
@@ -1022,31 +1101,10 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
     // ---- collect the window [wl, wu]; exact mass above it ----
     if (tid == 0) s.ctl->ncol = 0u;
     csync();
-    const int lane = tid & 31;
-    uint64_t accA = 0;
-    uint32_t kmn = 0xffffffffu, kmx = 0u;
     const float a0 = wl, a1 = wu;
-    for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
-        const bool inr = valid && x >= xlo && x <= xhi;
-        const bool in = inr && x >= a0 && x <= a1;
-        const uint64_t qa = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
-        accA += (inr && x > a1) ? qa : 0ull;
-        const uint32_t bal = __ballot_sync(0xffffffffu, in);
-        if (bal) {
-            const int lead = __ffs(bal) - 1;
-            uint32_t b0 = 0u;
-            if (lane == lead) b0 = atoms_add(&s.ctl->ncol, (uint32_t)__popc(bal));
-            b0 = __shfl_sync(0xffffffffu, b0, lead);
-            if (in) {
-                const uint32_t k = fkey(ydiv(p, x));
-                const uint32_t pos = slot0 + b0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
-                if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = k; s.cid[pos] = (uint32_t)c; }
-                kmn = min(kmn, k);
-                kmx = max(kmx, k);
-            }
-        }
-    });
-    const uint64_t A = cons_sum_u64(accA, s, tid);
+    const WCol wc = wpass_collect<DT>(P, tid, r, a0, a1, xlo, xhi, cxx, nmy, scale, slot0);
+    uint32_t kmn = wc.kmn, kmx = wc.kmx;
+    const uint64_t A = cons_sum_u64(wc.acc, s, tid);
     kmn = cons_min_u32(kmn, s, tid);
     kmx = cons_max_u32(kmx, s, tid);
     const uint32_t ncol = s.ctl->ncol;
@@ -1372,14 +1430,28 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
     int shard_or = 0;
     bool split_redo = false;
     if (P.merge_g > 0) {
-        double zt = 0.0;
-        for (int j = 0; j < P.merge_g; ++j) {
-            const int64_t sj = (int64_t)r * P.merge_g + j;
-            thr_max = max(thr_max, __ldg(P.shard_thr + sj));
-            shard_or |= __ldg(P.shard_status + sj);
-            const double my = __ldg(P.shard_mz + 2 * sj), z = __ldg(P.shard_mz + 2 * sj + 1);
-            if (z > 0.0) zt += z * exp(my - (double)My);
+        // one lane of warp 0 per shard (merge_g <= 32)
+        if (tid < 32) {
+            double z = 0.0;
+            uint32_t th = 0u, so = 0u;
+            if (tid < P.merge_g) {
+                const int64_t sj = (int64_t)r * P.merge_g + tid;
+                th = __ldg(P.shard_thr + sj);
+                so = (uint32_t)__ldg(P.shard_status + sj);
+                const double my = __ldg(P.shard_mz + 2 * sj), zz = __ldg(P.shard_mz + 2 * sj + 1);
+                if (zz > 0.0) z = zz * exp(my - (double)My);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+            th = __reduce_max_sync(0xffffffffu, th);
+            so = __reduce_or_sync(0xffffffffu, so);
+            if (tid == 0) { s.redd[0] = z; s.red32[0] = th; s.red32[1] = so; }
         }
+        csync();
+        const double zt = s.redd[0];
+        thr_max = s.red32[0];
+        shard_or = (int)s.red32[1];
+        csync();
         if (p.zsum && Zq > 0.0) Zq = zt * (double)scale;
         // a shard whose columns are all -inf just has an empty set
         split_redo = (shard_or & (FG_ROW_ERROR_MASK & ~FG_ROW_ALL_MASKED)) != 0;
