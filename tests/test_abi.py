@@ -87,3 +87,12 @@ def test_noalloc_validation_without_gpu():
     a.batch = (1 << 30) + 1
     assert lib.fg_sample_noalloc(ctypes.byref(a), None) == _lib.FG_ESCRATCH
     assert "scratch" in lib.fg_strerror(_lib.FG_ESCRATCH).decode()
+
+
+def test_split_mode_validation_without_gpu():
+    lib = _lib.load()
+    for bad in (-1, 3, 100):
+        assert lib.fg_sample_set_split(bad) == _lib.FG_EINVAL
+    for mode in (0, 2, 1):   # ends on the default (automatic)
+        assert lib.fg_sample_set_split(mode) == _lib.FG_OK
+    assert _lib.FG_SAMPLE_WORKSPACE_BYTES >= 256 * 1024
