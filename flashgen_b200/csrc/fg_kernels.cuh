@@ -819,10 +819,13 @@ __device__ __forceinline__ Located locate(const KParams& P, const Smem& s, const
 constexpr int NW = 4 * NB;   // bins per level; the counts use the blo/bhi area (4 * NB words)
 constexpr int WDEPTH = 3;    // histogram levels before the fallback
 
+constexpr int NW0 = 2 * NW;  // level-0 bins when the free part of the candidate buffer can hold them
+
+template <int NBIN>
 __device__ __forceinline__ int wbin(float x, float xa, float inv) {
     const float t = (x - xa) * inv;
     if (!(t > 0.0f)) return 0;
-    return t >= (float)(NW - 1) ? NW - 1 : (int)t;
+    return t >= (float)(NBIN - 1) ? NBIN - 1 : (int)t;
 }
 
 struct WWin {
@@ -833,9 +836,10 @@ struct WWin {
 
 // One level: bins over [wl, wu] (x), counts in cnt. Returns the bins whose
 // bracketed cumulative mass, descending from `above`, straddles T.
+template <int NBIN>
 __device__ WWin wscan(const Smem& s, const uint32_t* cnt, float wl, float wu, float inv, double sx,
                       const RowParams& p, float My, double scale, double above, double T, int tid) {
-    constexpr int PER = NW / NCT;
+    constexpr int PER = NBIN / NCT;
     const int lane = tid & 31, wid = tid >> 5;
     const double w = inv > 0.0f ? 1.0 / (double)inv : 0.0;
     const double rT = p.temp_on ? 1.0 / (double)p.T : 1.0;
@@ -844,13 +848,13 @@ __device__ WWin wscan(const Smem& s, const uint32_t* cnt, float wl, float wu, fl
     double sl = 0.0, su = 0.0;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-        const int b = NW - 1 - (tid * PER + j);   // thread order = descending bins
+        const int b = NBIN - 1 - (tid * PER + j);   // thread order = descending bins
         c[j] = cnt[b];
         lq[j] = 0.0;
         uq[j] = 0.0;
         if (c[j]) {
             double e0 = (b == 0 || w == 0.0) ? (double)wl : (double)wl + (double)b * w - sx;
-            double e1 = (b == NW - 1 || w == 0.0) ? (double)wu : (double)wl + (double)(b + 1) * w + sx;
+            double e1 = (b == NBIN - 1 || w == 0.0) ? (double)wu : (double)wl + (double)(b + 1) * w + sx;
             e0 = fmax(e0, (double)wl) * rT;
             e1 = fmin(e1, (double)wu) * rT;
             e0 -= fabs(e0) * 2.4e-7;   // y = fl(x / T)
@@ -878,10 +882,10 @@ __device__ WWin wscan(const Smem& s, const uint32_t* cnt, float wl, float wu, fl
         if (i < wid) { bl += s.redd[i]; bu += __longlong_as_double((long long)s.red64[i]); }
     csync();
     double pl = bl + il - sl, pu = bu + iu - su;
-    int bmax = -1, bmin = NW;
+    int bmax = -1, bmin = NBIN;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-        const int b = NW - 1 - (tid * PER + j);
+        const int b = NBIN - 1 - (tid * PER + j);
         const double exL = (above + pl) * (1.0 - 1e-12) - 2.0;
         const double inU = (above + pu + uq[j]) * (1.0 + 1e-12) + 2.0;
         if (c[j] && exL <= T && T < inU) { bmax = max(bmax, b); bmin = min(bmin, b); }
@@ -897,7 +901,7 @@ __device__ WWin wscan(const Smem& s, const uint32_t* cnt, float wl, float wu, fl
     uint64_t cc = 0;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-        const int b = NW - 1 - (tid * PER + j);
+        const int b = NBIN - 1 - (tid * PER + j);
         if (out.any && b >= out.lo && b <= out.hi) cc += c[j];
     }
     out.count = (uint32_t)cons_sum_u64(cc, s, tid);
@@ -925,14 +929,17 @@ struct WLoc {
 // The passes of the windowed locate, each its own function with scalar
 // arguments: the per-element loop then keeps its few values in registers
 // instead of reloading the caller's spilled state for every element.
-template <int DT>
-__device__ __noinline__ void wpass_count(const KParams& P, int tid, int r, float a0, float bi, float xlo, float xhi) {
+// Level-0 counts: NW0 bins in the candidate buffer's free part from slot0,
+// else NW bins in the blo/bhi area.
+template <int DT, int NBIN>
+__device__ __noinline__ void wpass_count(const KParams& P, int tid, int r, float a0, float bi, float xlo, float xhi,
+                                         uint32_t slot0) {
     const Smem s = carve(smem_base(), P);
     const RowParams p = row_params(P, r);
     const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
-    uint32_t* cnt = s.blo;
+    uint32_t* cnt = NBIN == NW0 ? s.ckey + slot0 : s.blo;
     for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
-        if (valid && x >= a0 && x <= xhi && x >= xlo) reds_add(&cnt[wbin(x, a0, bi)], 1u);
+        if (valid && x >= a0 && x <= xhi && x >= xlo) reds_add(&cnt[wbin<NBIN>(x, a0, bi)], 1u);
     });
 }
 // Mass above the window (per thread), counts inside it. Branch-free per
@@ -950,7 +957,7 @@ __device__ __noinline__ uint64_t wpass_mass(const KParams& P, int tid, int r, fl
         const bool inr = valid && x >= xlo && x <= xhi;
         const uint64_t q = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
         acc += (inr && x > a1) ? q : 0ull;
-        if (inr && x <= a1 && x >= a0) reds_add(&cnt[wbin(x, a0, bi)], 1u);
+        if (inr && x <= a1 && x >= a0) reds_add(&cnt[wbin<NW>(x, a0, bi)], 1u);
     });
     return acc;
 }
@@ -1034,30 +1041,37 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
     uint64_t above = 0;
     bool beyond = false, single = false;
     for (int d = 0;; ++d) {
+        // level 0 spans the whole region: twice the bins when the candidate
+        // buffer's free part holds them (the collection overwrites them later)
+        const bool big = d == 0 && room >= (uint32_t)NW0 + 64u;
+        const int nb = big ? NW0 : NW;
+        uint32_t* cl = big ? s.ckey + slot0 : cnt;
         const float span = wu - wl;
-        float inv = span > 0.0f ? (float)NW / span : 0.0f;
+        float inv = span > 0.0f ? (float)nb / span : 0.0f;
         if (!(inv < INFINITY)) inv = 0.0f;
         const double sx = 1e-6 * (double)span;
-        for (int i = tid; i < NW; i += NCT) cnt[i] = 0u;
+        for (int i = tid; i < nb; i += NCT) cl[i] = 0u;
         csync();
         uint64_t acc = 0;
         const float a0 = wl, a1 = wu, bi = inv;
         if (d == 0) {
             // nothing lies above level 0's range: counts only
-            wpass_count<DT>(P, tid, r, a0, bi, xlo, xhi);
+            if (big) wpass_count<DT, NW0>(P, tid, r, a0, bi, xlo, xhi, slot0);
+            else wpass_count<DT, NW>(P, tid, r, a0, bi, xlo, xhi, slot0);
         } else {
             acc = wpass_mass<DT>(P, tid, r, a0, a1, bi, xlo, xhi, cxx, nmy, scale);
         }
         csync();
         if (d > 0) above = cons_sum_u64(acc, s, tid);
-        const WWin win = wscan(s, cnt, wl, wu, inv, sx, p, My, sc, (double)above, T, tid);
+        const WWin win = big ? wscan<NW0>(s, cl, wl, wu, inv, sx, p, My, sc, (double)above, T, tid)
+                             : wscan<NW>(s, cl, wl, wu, inv, sx, p, My, sc, (double)above, T, tid);
         if (!win.any) { beyond = true; break; }
         // the window's x-range, widened by the slack, closed under equal y
         const double w = inv > 0.0f ? 1.0 / (double)inv : 0.0;
         float nl = wl, nu = wu;
         if (w > 0.0) {
             if (win.lo > 0) nl = __double2float_rd((double)wl + (double)win.lo * w - sx);
-            if (win.hi < NW - 1) nu = __double2float_ru((double)wl + (double)(win.hi + 1) * w + sx);
+            if (win.hi < nb - 1) nu = __double2float_ru((double)wl + (double)(win.hi + 1) * w + sx);
         }
         nl = fmaxf(wl, x_lower(p, fkey(ydiv(p, nl))));
         nu = fminf(wu, x_upper(p, fkey(ydiv(p, nu))));
