@@ -978,23 +978,26 @@ __device__ __noinline__ WRun wpass_run(const KParams& P, int tid, int r, float a
     });
     return w;
 }
-struct WCol { uint64_t acc; uint32_t kmn, kmx; };
-// Collects the window [a0, a1] into the buffer from slot0 (counter
-// ctl->ncol, zero on entry); per thread, the mass above the window and the
-// key range collected.
+struct WCol { uint64_t acc, acc2; uint32_t kmn, kmx, kmn2, kmx2; };
+// Collects the window [a0, a1], and the window [b0, b1] above it when b0 <=
+// b1, into the buffer from slot0 (counter ctl->ncol, zero on entry); per
+// thread, the mass above each window and the key range collected of each.
 template <int DT>
 __device__ __noinline__ WCol wpass_collect(const KParams& P, int tid, int r, float a0, float a1, float xlo, float xhi,
-                                           float cxx, float nmy, float scale, uint32_t slot0) {
+                                           float cxx, float nmy, float scale, uint32_t slot0, float b0, float b1) {
     const Smem s = carve(smem_base(), P);
     const RowParams p = row_params(P, r);
     const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
     const int lane = tid & 31;
-    WCol w{0ull, 0xffffffffu, 0u};
+    WCol w{0ull, 0ull, 0xffffffffu, 0u, 0xffffffffu, 0u};
     for_row<DT>(P, s, p, r, g, tid, [&](bool valid, int c, float x) {
         const bool inr = valid && x >= xlo && x <= xhi;
-        const bool in = inr && x >= a0 && x <= a1;
+        const bool inA = inr && x >= a0 && x <= a1;
+        const bool inB = inr && x >= b0 && x <= b1;
+        const bool in = inA || inB;
         const uint64_t qa = q_of(ex2_approx(__fmaf_rn(x, cxx, nmy)), scale);
         w.acc += (inr && x > a1) ? qa : 0ull;
+        w.acc2 += (inr && x > b1) ? qa : 0ull;
         const uint32_t bal = __ballot_sync(0xffffffffu, in);
         if (bal) {
             const int lead = __ffs(bal) - 1;
@@ -1005,8 +1008,8 @@ __device__ __noinline__ WCol wpass_collect(const KParams& P, int tid, int r, flo
                 const uint32_t k = fkey(ydiv(p, x));
                 const uint32_t pos = slot0 + b0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
                 if (pos < (uint32_t)CAND_CAP) { s.ckey[pos] = k; s.cid[pos] = (uint32_t)c; }
-                w.kmn = min(w.kmn, k);
-                w.kmx = max(w.kmx, k);
+                if (inA) { w.kmn = min(w.kmn, k); w.kmx = max(w.kmx, k); }
+                else { w.kmn2 = min(w.kmn2, k); w.kmx2 = max(w.kmx2, k); }
             }
         }
     });
@@ -1016,10 +1019,11 @@ __device__ __noinline__ WCol wpass_collect(const KParams& P, int tid, int r, flo
 template <int DT>
 __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g, int tid,
                         uint32_t rlo, uint32_t rhi, float ylo, float yhi, uint64_t target, float My, float scale,
-                        uint32_t slot0) {
+                        uint32_t slot0, uint64_t target2) {
     WLoc W;
     Located& L = W.L;
     W.fallback = false;
+    if (tid == 0) s.ctl->b_ok = 0u;
     L.ok = false; L.in_buffer = false; L.key = 0u; L.before = 0; L.at = 0; L.n_at = 0; L.total = 0;
     L.n0 = slot0; L.n1 = slot0;
     if (rlo > rhi) return W;
@@ -1040,6 +1044,10 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
     const double T = (double)target;
     uint64_t above = 0;
     bool beyond = false, single = false;
+    // second window (level 0 only): the draw's, for target2 < target
+    bool b_try = false;
+    float bl = 1.0f, bu = 0.0f;
+    uint32_t bcount = 0u, acount = 0u;
     for (int d = 0;; ++d) {
         // level 0 spans the whole region: twice the bins when the candidate
         // buffer's free part holds them (the collection overwrites them later)
@@ -1066,8 +1074,22 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
         const WWin win = big ? wscan<NW0>(s, cl, wl, wu, inv, sx, p, My, sc, (double)above, T, tid)
                              : wscan<NW>(s, cl, wl, wu, inv, sx, p, My, sc, (double)above, T, tid);
         if (!win.any) { beyond = true; break; }
-        // the window's x-range, widened by the slack, closed under equal y
         const double w = inv > 0.0f ? 1.0 / (double)inv : 0.0;
+        if (d == 0 && target2 < target) {
+            const WWin w2 = big ? wscan<NW0>(s, cl, wl, wu, inv, sx, p, My, sc, 0.0, (double)target2, tid)
+                                : wscan<NW>(s, cl, wl, wu, inv, sx, p, My, sc, 0.0, (double)target2, tid);
+            if (w2.any && w > 0.0) {
+                float l2 = wl, u2 = wu;
+                if (w2.lo > 0) l2 = __double2float_rd((double)wl + (double)w2.lo * w - sx);
+                if (w2.hi < nb - 1) u2 = __double2float_ru((double)wl + (double)(w2.hi + 1) * w + sx);
+                bl = fmaxf(wl, x_lower(p, fkey(ydiv(p, l2))));
+                bu = fminf(wu, x_upper(p, fkey(ydiv(p, u2))));
+                bcount = w2.count;
+                b_try = bu >= bl;
+            }
+        }
+        acount = win.count;
+        // the window's x-range, widened by the slack, closed under equal y
         float nl = wl, nu = wu;
         if (w > 0.0) {
             if (win.lo > 0) nl = __double2float_rd((double)wl + (double)win.lo * w - sx);
@@ -1116,7 +1138,11 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
     if (tid == 0) s.ctl->ncol = 0u;
     csync();
     const float a0 = wl, a1 = wu;
-    const WCol wc = wpass_collect<DT>(P, tid, r, a0, a1, xlo, xhi, cxx, nmy, scale, slot0);
+    // the draw's window rides along when it lies wholly above this one and
+    // both fit the free buffer
+    const bool use_b = b_try && bl > a1 && acount + bcount <= fit;
+    const WCol wc = wpass_collect<DT>(P, tid, r, a0, a1, xlo, xhi, cxx, nmy, scale, slot0, use_b ? bl : 1.0f,
+                                      use_b ? bu : 0.0f);
     uint32_t kmn = wc.kmn, kmx = wc.kmx;
     const uint64_t A = cons_sum_u64(wc.acc, s, tid);
     kmn = cons_min_u32(kmn, s, tid);
@@ -1124,9 +1150,23 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
     const uint32_t ncol = s.ctl->ncol;
     if (ncol > room) { W.fallback = true; return W; }
     const uint32_t n1 = slot0 + ncol;
-    uint64_t wloc = 0;
-    for (uint32_t i = slot0 + tid; i < n1; i += NCT) wloc += q_of(efast(funkey(s.ckey[i]), My), scale);
+    uint64_t wloc = 0, wloc2 = 0;
+    for (uint32_t i = slot0 + tid; i < n1; i += NCT) {
+        const uint32_t k = s.ckey[i];
+        const uint64_t q = q_of(efast(funkey(k), My), scale);
+        if (k <= kmx) wloc += q; else wloc2 += q;
+    }
     const uint64_t Wm = cons_sum_u64(wloc, s, tid);
+    if (use_b) {
+        const uint64_t A2 = cons_sum_u64(wc.acc2, s, tid);
+        const uint64_t W2 = cons_sum_u64(wloc2, s, tid);
+        const uint32_t k2n = cons_min_u32(wc.kmn2, s, tid);
+        const uint32_t k2x = cons_max_u32(wc.kmx2, s, tid);
+        if (tid == 0 && W2 > 0 && k2n > kmx && k2n <= k2x) {
+            s.ctl->b_ok = 1u; s.ctl->b_klo = k2n; s.ctl->b_khi = k2x; s.ctl->b_n1 = n1;
+            s.ctl->b_above = A2; s.ctl->b_mass = W2;
+        }
+    }
     if (target < A) { W.fallback = true; return W; }   // bracket violated: take the exact path
     if (target >= A + Wm) {
         // past the window: only when the target is past the region's total
@@ -1138,8 +1178,8 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
         [&](auto&& f) {
             for (uint32_t i0 = slot0; i0 < n1; i0 += NCT) {
                 const uint32_t i = i0 + tid;
-                const bool v = i < n1;
-                const uint32_t k = v ? s.ckey[i] : 0u;
+                const uint32_t k = i < n1 ? s.ckey[i] : 0u;
+                const bool v = i < n1 && k <= kmx;
                 f(v, k, v ? q_of(efast(funkey(k), My), scale) : 0ull);
             }
         },
@@ -1157,11 +1197,12 @@ __device__ __forceinline__ WLoc wlocate(const KParams& P, const Smem& s, const R
 // streaming loop has its address taken, so it stays in registers.
 template <int DT>
 __device__ __noinline__ WLoc wlocate_cold(const KParams& P, int tid, int r, uint32_t rlo, uint32_t rhi, float ylo,
-                                          float yhi, uint64_t target, float My, float scale, uint32_t slot0) {
+                                          float yhi, uint64_t target, float My, float scale, uint32_t slot0,
+                                          uint64_t target2) {
     const Smem s = carve(smem_base(), P);
     const RowParams p = row_params(P, r);
     const RowGeom g = row_geom<Elem<DT>::SIZE>(P, r);
-    return wlocate<DT>(P, s, p, r, g, tid, rlo, rhi, ylo, yhi, target, My, scale, slot0);
+    return wlocate<DT>(P, s, p, r, g, tid, rlo, rhi, ylo, yhi, target, My, scale, slot0, target2);
 }
 template <int DT>
 __device__ __noinline__ Located locate_cold(const KParams& P, int tid, int r, uint32_t rlo, uint32_t rhi, float ylo,
@@ -1183,13 +1224,14 @@ __device__ __noinline__ uint64_t region_mass_cold(const KParams& P, int tid, int
 template <int DT>
 __device__ __forceinline__ Located locate_fast(const KParams& P, const Smem& s, const RowParams& p, int r, const RowGeom& g,
                                int tid, uint32_t rlo, uint32_t rhi, float ylo, float yhi, uint64_t target, float My,
-                               float scale, uint32_t slot0, bool clamp) {
-    (void)s; (void)p; (void)g;
-    WLoc w = wlocate_cold<DT>(P, tid, r, rlo, rhi, ylo, yhi, target, My, scale, slot0);
+                               float scale, uint32_t slot0, bool clamp, uint64_t target2 = ~0ull) {
+    (void)p; (void)g;
+    WLoc w = wlocate_cold<DT>(P, tid, r, rlo, rhi, ylo, yhi, target, My, scale, slot0, target2);
     // like locate(), a clamped call answers a target past the total with the last element
     if (clamp && !w.fallback && !w.L.ok && w.L.total > 0 && target >= w.L.total)
-        w = wlocate_cold<DT>(P, tid, r, rlo, rhi, ylo, yhi, w.L.total - 1, My, scale, slot0);
+        w = wlocate_cold<DT>(P, tid, r, rlo, rhi, ylo, yhi, w.L.total - 1, My, scale, slot0, ~0ull);
     if (!w.fallback) return w.L;
+    if (tid == 0) s.ctl->b_ok = 0u;   // the exact path reuses the buffer
     return locate_cold<DT>(P, tid, r, rlo, rhi, ylo, yhi, target, My, scale, slot0);
 }
 
@@ -1723,7 +1765,15 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
             } else {
                 status |= FG_ROW_GENERAL_PATH;
                 const uint64_t tr = Pt >= AC ? Pt - AC : 0ull;
-                const Located L = locate_fast<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, tr, My, scale, nC, false);
+                // the draw's target, predicted from Pt (the final Qf exceeds Pt by
+                // less than one element's mass), so its window can be collected
+                // in the same pass as the cut's
+                uint64_t t2p = ~0ull;
+                {
+                    const uint64_t tg = (uint64_t)floor((double)p.u * (double)Pt);
+                    if (tg >= AC && tg - AC < tr) t2p = tg - AC;
+                }
+                const Located L = locate_fast<DT>(P, s, p, r, g, tid, rlo, rhi, yRlo, yRhi, tr, My, scale, nC, false, t2p);
                 if (!L.ok || tr >= L.total) {
                     cut = false;               // the cut lies below every element: keep all
                     Qf = AC + L.total;
@@ -1780,6 +1830,33 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
             } else {
                 status |= FG_ROW_GENERAL_PATH;
                 const uint64_t t2 = target - (nC > 0 ? AC : 0ull);
+                bool drawn = false;
+                if (cut_in_R && ctl->b_ok) {
+                    const uint32_t bk0 = ctl->b_klo, bk1 = ctl->b_khi, bn1 = ctl->b_n1;
+                    const uint64_t bA = ctl->b_above, bW = ctl->b_mass;
+                    if (t2 >= bA && t2 - bA < bW) {
+                        // inside the window collected with the cut's
+                        const SelOut sb = block_select<true, false>(
+                            [&](auto&& f) {
+                                for (uint32_t i0 = nC; i0 < bn1; i0 += NCT) {
+                                    const uint32_t i = i0 + tid;
+                                    const uint32_t k = i < bn1 ? s.ckey[i] : 0u;
+                                    const bool v = i < bn1 && k >= bk0 && k <= bk1;
+                                    f(v, k, v ? q_of(efast(funkey(k), My), scale) : 0ull);
+                                }
+                            },
+                            t2 - bA, bk0, varying_bits(bk0, bk1), s, tid);
+                        if (sb.ok) {
+                            const uint64_t qd = sb.n_at ? sb.at / sb.n_at : 0;
+                            uint64_t j = qd ? (t2 - bA - sb.before) / qd : 0;
+                            if (j >= sb.n_at) j = sb.n_at ? sb.n_at - 1 : 0;
+                            out_id = jth_id(P, s, tid, nC, bn1, sb.key, sb.n_at, j);
+                            dkey = sb.key;
+                            drawn = true;
+                        }
+                    }
+                }
+                if (!drawn) {
                 const uint32_t rlo2 = cut_in_R ? tstar : rlo;
                 const float ylo2 = cut_in_R ? fmaxf(funkey(tstar), My - 64.0f) : yRlo;
                 const Located L = locate_fast<DT>(P, s, p, r, g, tid, rlo2, rhi, ylo2, yRhi, t2, My, scale, nC, true);
@@ -1790,6 +1867,7 @@ __device__ __forceinline__ void finish_row(const KParams& P, const Smem& s, cons
                     out_id = L.in_buffer ? jth_id(P, s, tid, L.n0, L.n1, L.key, L.n_at, j)
                                          : jth_id_row<DT>(P, s, p, r, g, tid, L.key, j);
                 }
+                }   // !drawn
             }
         }
         // merge stage: exact only when the decision lies in the union's

@@ -126,6 +126,10 @@ struct RowCtl {
     uint32_t preq;           // passes over the current row requested from the producer
     uint32_t rst, rph;       // consumers' ring position between passes
     SelSlot sel[2];          // select results, alternating between passes
+    // a second window collected with the top-p cut's window (the draw's, from
+    // its predicted target): keys [b_klo, b_khi] in [slot0, b_n1) of the buffer
+    uint32_t b_ok, b_klo, b_khi, b_n1;
+    unsigned long long b_above, b_mass;
 };
 
 struct Smem {
