@@ -332,7 +332,7 @@ def main():
         a.top_k, a.greedy = packed.top_k.data_ptr(), packed.greedy.data_ptr()
         a.uniforms = uni[i].data_ptr()
         a.out_ids, a.out_status = out.data_ptr(), status.data_ptr()
-        a.workspace = wspace.data_ptr()
+        _lib.set_workspace(a, wspace)
         return a
 
     argv = [make_args(0), make_args(1)]

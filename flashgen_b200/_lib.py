@@ -26,7 +26,8 @@ FG_ROW_ERROR_MASK = 0x00FF
 FG_ROW_GENERAL_PATH = 0x0100
 FG_ROW_GREEDY = 0x0200
 
-EXPORTED_SYMBOLS = ("fg_sample", "fg_sample_candidates", "fg_sample_noalloc", "fg_sample_set_split",
+EXPORTED_SYMBOLS = ("fg_sample", "fg_sample_workspace_size", "fg_sample_candidates", "fg_sample_noalloc",
+                    "fg_sample_set_split",
                     "fg_apply_repetition_penalty", "fg_argmax", "fg_strerror", "fg_version")
 
 
@@ -56,10 +57,12 @@ class FgSampleArgs(ctypes.Structure):
         ("out_status", ctypes.c_void_p),
         ("out_probs", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
 FG_SAMPLE_WORKSPACE_BYTES = 262144
+FG_SAMPLE_WORKSPACE_MIN_BYTES = 256
 
 
 _lib = None
@@ -86,6 +89,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib = ctypes.CDLL(path)
         lib.fg_sample.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p]
         lib.fg_sample.restype = ctypes.c_int
+        lib.fg_sample_workspace_size.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
+        lib.fg_sample_workspace_size.restype = ctypes.c_size_t
         lib.fg_sample_candidates.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p, ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
         lib.fg_sample_candidates.restype = ctypes.c_int
@@ -106,6 +111,12 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.fg_version.restype = ctypes.c_int
         _lib = lib
         return lib
+
+
+def set_workspace(a: FgSampleArgs, ws) -> None:
+    """Point ``a`` at a device workspace tensor and record its size."""
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = ws.numel() * ws.element_size()
 
 
 def check(rc: int, what: str) -> None:

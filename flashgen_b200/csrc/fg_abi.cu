@@ -4,6 +4,7 @@
 // launches; it does no work proportional to batch * vocab, allocates nothing
 // and never synchronises the stream.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "fg_kernels.cuh"
@@ -73,7 +74,7 @@ int launch_sample(const fg::KParams& P, int smem, int grid, cudaStream_t st, Dev
 
 extern "C" {
 
-int fg_version(void) { return 100; }
+int fg_version(void) { return 200; }
 
 const char* fg_strerror(int code) {
     switch (code) {
@@ -90,6 +91,8 @@ const char* fg_strerror(int code) {
 }  // extern "C"
 
 namespace {
+constexpr int32_t kMaxBatch = 1 << 30;
+
 // Shared-memory layout for P (vocab, pen_possible, hu_cap set), then the
 // launch. mass_vocab: how many elements a row's total mass may sum (the merge
 // of the split path sums a whole row's mass over a shorter union row).
@@ -155,7 +158,8 @@ int layout_and_launch(fg::KParams& P, int dtype, DevInfo* d, cudaStream_t st, in
 constexpr int kSplitCand = 256;        // candidates per shard (<= 2 * NB)
 constexpr int kSplitMinCols = 4096;    // shard width below which splitting does not pay
 constexpr size_t kSplitScratch0 = 4096;
-int g_split_mode = 1;                  // 0 off, 1 automatic, 2 whenever the shapes allow
+// 0 off, 1 automatic, 2 whenever the shapes allow; process-wide, read once per call
+std::atomic<int> g_split_mode{1};
 
 size_t split_bytes(int64_t B, int G) {
     const int64_t n = B * G;
@@ -163,15 +167,18 @@ size_t split_bytes(int64_t B, int G) {
 }
 
 int split_shards(const FgSampleArgs* a, int64_t vtot, const DevInfo* d) {
-    if (g_split_mode == 0 || a->out_probs != nullptr) return 0;
+    const int mode = g_split_mode.load(std::memory_order_relaxed);
+    if (mode == 0 || a->out_probs != nullptr) return 0;
     if (a->vocab_offset != 0 || vtot != a->vocab) return 0;
     if (a->batch > 1 && a->row_stride != a->vocab) return 0;
     for (int G = 32; G >= 4; G >>= 1) {
         if (a->vocab % G != 0) continue;
         const int W = a->vocab / G;
         if (W < 32) continue;
-        if (g_split_mode == 1 && (W < kSplitMinCols || (int64_t)a->batch * G > d->sms)) continue;
+        if (mode == 1 && (W < kSplitMinCols || (int64_t)a->batch * G > d->sms)) continue;
+        // the caller's buffer must hold the scratch (a smaller one only turns the path off)
         if (split_bytes(a->batch, G) > (size_t)FG_SAMPLE_WORKSPACE_BYTES) continue;
+        if (split_bytes(a->batch, G) > a->workspace_bytes) continue;
         return G;
     }
     return 0;
@@ -235,11 +242,14 @@ int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* ci
     if (a->temperature == nullptr || a->top_p == nullptr || a->top_k == nullptr || a->uniforms == nullptr ||
         a->out_ids == nullptr || a->workspace == nullptr)
         return FG_EINVAL;
+    if (a->workspace_bytes < (size_t)FG_SAMPLE_WORKSPACE_MIN_BYTES) return FG_EINVAL;
     if ((a->hist_ids == nullptr) != (a->hist_offsets == nullptr)) return FG_EINVAL;
     if (a->vocab_offset < 0) return FG_EINVAL;
     const int64_t vtot = a->vocab_total > 0 ? a->vocab_total : a->vocab;
     if (vtot < a->vocab_offset + a->vocab) return FG_EINVAL;
     if (a->vocab > (1 << 28)) return FG_ENOTSUP;
+    // the row queue's 32-bit counter runs to about 2 * batch plus one claim per CTA
+    if (a->batch > kMaxBatch) return FG_ENOTSUP;
     if (a->batch == 0) return FG_OK;
 
     DevInfo* d = nullptr;
@@ -280,8 +290,20 @@ int fg_sample(const FgSampleArgs* a, void* stream) {
 
 int fg_sample_set_split(int mode) {
     if (mode < 0 || mode > 2) return FG_EINVAL;
-    g_split_mode = mode;
+    g_split_mode.store(mode, std::memory_order_relaxed);
     return FG_OK;
+}
+
+size_t fg_sample_workspace_size(int32_t batch, int32_t vocab, int32_t dtype) {
+    if (elem_size(dtype) == 0 || batch < 0 || vocab < 1 || batch > kMaxBatch) return 0;
+    // the largest split scratch any shard count G may use for this shape
+    size_t need = (size_t)FG_SAMPLE_WORKSPACE_MIN_BYTES;
+    for (int G = 32; G >= 4; G >>= 1) {
+        if (vocab % G != 0 || vocab / G < 32) continue;
+        const size_t b = split_bytes(batch, G);
+        if (b <= (size_t)FG_SAMPLE_WORKSPACE_BYTES) need = std::max(need, b);
+    }
+    return need;
 }
 
 int fg_sample_candidates(const FgSampleArgs* a, float* vals, int32_t* gids, int32_t* counts, int32_t cand_max,
@@ -296,9 +318,11 @@ int fg_sample_candidates(const FgSampleArgs* a, float* vals, int32_t* gids, int3
 // allocation there can synchronise the device or fail mid-step), and a host
 // that binds the library through a plain FFI with no device allocator of its
 // own. The row-queue counters live in a file-scope __device__ array instead
-// (one per device context). Its address is looked up once per device, on the
-// first call with that device current, which also clears it on the call's
-// stream; make that first call before any stream capture. Every launch
+// (one per device context). Its address is looked up once per device
+// context, on the first call with that device current, which also clears it on
+// the call's stream; make that first call before any stream capture. A device
+// reset (cudaDeviceReset) ends the context: the next call sees a new context
+// id, looks the address up again and clears the array again. Every launch
 // leaves the counters zero again. Calls that overlap on the GPU (different
 // streams) share the counters and race: serialise them.
 // ---------------------------------------------------------------------------
@@ -306,8 +330,41 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 256;
 constexpr int32_t kNoAllocMaxBatch = 1 << 30;   // the queue counter runs to about 2 * batch in 32 bits
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-void* g_noalloc_ptr[kMaxDevices] = {};
+struct NoAllocSlot {
+    unsigned long long ctx_id = 0;   // driver context id the address belongs to (0: none yet)
+    void* ptr = nullptr;
+};
+NoAllocSlot g_noalloc[kMaxDevices];
 static_assert(sizeof(fg::Workspace) <= kNoAllocScratchBytes, "static scratch smaller than the row-queue counters");
+
+// Unique id of the current driver context (cuCtxGetCurrent + cuCtxGetId,
+// reached through the runtime's driver entry points, so the library links no
+// libcuda symbol directly). 0 when it cannot be read.
+using CtxGetCurrentFn = int (*)(void**);
+using CtxGetIdFn = int (*)(void*, unsigned long long*);
+unsigned long long current_ctx_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static bool looked_up = false;
+    if (!looked_up) {
+        void* f0 = nullptr;
+        void* f1 = nullptr;
+        cudaDriverEntryPointQueryResult q0, q1;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f0, 12000, cudaEnableDefault, &q0) == cudaSuccess &&
+            q0 == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(f0);
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f1, 12000, cudaEnableDefault, &q1) == cudaSuccess &&
+            q1 == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(f1);
+        looked_up = true;
+    }
+    if (get_current == nullptr || get_id == nullptr) return 0;
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current(&ctx) != 0 || ctx == nullptr) return 0;
+    if (get_id(ctx, &id) != 0) return 0;
+    return id;
+}
 }  // namespace
 
 int fg_sample_noalloc(const FgSampleArgs* a, void* stream) {
@@ -318,17 +375,27 @@ int fg_sample_noalloc(const FgSampleArgs* a, void* stream) {
     void* ws = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
-        if (g_noalloc_ptr[dev] == nullptr) {
+        NoAllocSlot& slot = g_noalloc[dev];
+        unsigned long long id = current_ctx_id();   // 0 before the runtime made a context
+        if (slot.ptr == nullptr || id != slot.ctx_id) {
             void* p = nullptr;
+            // set-up: the symbol's device address in the current context (the
+            // runtime creates or attaches the device's primary context here)
             if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return FG_EDEVICE;
-            if (cudaMemsetAsync(p, 0, kNoAllocScratchBytes, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
-                return FG_EDEVICE;
-            g_noalloc_ptr[dev] = p;
+            id = current_ctx_id();
+            if (p != slot.ptr || id != slot.ctx_id) {
+                if (cudaMemsetAsync(p, 0, kNoAllocScratchBytes, reinterpret_cast<cudaStream_t>(stream)) !=
+                    cudaSuccess)
+                    return FG_EDEVICE;
+            }
+            slot.ptr = p;
+            slot.ctx_id = id;
         }
-        ws = g_noalloc_ptr[dev];
+        ws = slot.ptr;
     }
     FgSampleArgs b = *a;
     b.workspace = ws;
+    b.workspace_bytes = kNoAllocScratchBytes;
     // the fixed scratch holds the row-queue counters only: no split path
     return sample_launch(&b, stream, nullptr, nullptr, nullptr, 0, false);
 }

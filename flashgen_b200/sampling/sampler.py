@@ -131,7 +131,7 @@ def fused_sample(logits: torch.Tensor, packed: PackedParams, uniforms: torch.Ten
     st = stream if stream is not None else torch.cuda.current_stream(logits.device)
     if workspace is None:
         workspace = workspace_for(logits.device, st)
-    a.workspace = workspace.data_ptr()
+    _lib.set_workspace(a, workspace)
     with torch.cuda.device(logits.device):
         _lib.check(lib.fg_sample(a, st.cuda_stream), "fg_sample")
     return out

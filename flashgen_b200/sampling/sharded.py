@@ -74,7 +74,7 @@ def local_candidates(shard: torch.Tensor, packed: PackedParams, uniforms: torch.
     a.uniforms = uniforms.data_ptr()
     a.out_ids, a.out_status = out.data_ptr(), status.data_ptr()
     st = stream if stream is not None else torch.cuda.current_stream(dev)
-    a.workspace = workspace_for(dev, st).data_ptr()
+    _lib.set_workspace(a, workspace_for(dev, st))
     with torch.cuda.device(dev):
         _lib.check(lib.fg_sample_candidates(a, vals.data_ptr(), gids.data_ptr(), counts.data_ptr(), cand_max,
                                             st.cuda_stream), "fg_sample_candidates")

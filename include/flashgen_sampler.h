@@ -123,19 +123,26 @@ typedef struct FgSampleArgs {
     int32_t*       out_status;          /* [B] or NULL                             */
     float*         out_probs;           /* [B, vocab] kept-set probabilities, 0
                                            elsewhere (debug/oracle mode) or NULL   */
-    void*          workspace;           /* FG_SAMPLE_WORKSPACE_BYTES of device
-                                           memory, zero before the first call       */
+    void*          workspace;           /* device scratch, zero before the first
+                                           call (see below)                         */
+    size_t         workspace_bytes;     /* size of `workspace` in bytes            */
 } FgSampleArgs;
 
 /*
  * Workspace: rows are handed to the GPU's persistent CTAs through counters in
- * the first 256 bytes of this device buffer. The caller zeroes the buffer once
- * (cudaMemset) before its first use; every fg_sample call leaves the counters
- * zero again. The rest is scratch for small batches, whose rows fg_sample cuts
- * into column shards sampled by several CTAs (see fg_sample_set_split). Calls
- * that may run concurrently on the GPU (different streams) need separate
- * workspaces.
+ * the first FG_SAMPLE_WORKSPACE_MIN_BYTES of this device buffer. The caller
+ * zeroes the buffer once (cudaMemset) before its first use; every fg_sample
+ * call leaves the counters zero again. Bytes beyond the counters are scratch
+ * for small batches, whose rows fg_sample cuts into column shards sampled by
+ * several CTAs (see fg_sample_set_split): that path runs only when
+ * workspace_bytes covers its scratch, so a smaller buffer is always safe and
+ * only gives up that speed-up. fg_sample_workspace_size(batch, vocab, dtype)
+ * gives the size that lets every path run; FG_SAMPLE_WORKSPACE_BYTES is an
+ * upper bound of it for any shape. workspace_bytes below
+ * FG_SAMPLE_WORKSPACE_MIN_BYTES returns FG_EINVAL. Calls that may run
+ * concurrently on the GPU (different streams) need separate workspaces.
  */
+#define FG_SAMPLE_WORKSPACE_MIN_BYTES 256
 #define FG_SAMPLE_WORKSPACE_BYTES 262144
 
 /*
@@ -145,6 +152,14 @@ typedef struct FgSampleArgs {
  * `stream` is a cudaStream_t (NULL = legacy default stream).
  */
 int fg_sample(const FgSampleArgs* args, void* stream);
+
+/*
+ * Bytes of workspace with which fg_sample may use every path for a batch of
+ * this shape (FG_SAMPLE_WORKSPACE_MIN_BYTES when only the counters are
+ * needed); 0 for an invalid shape or dtype. Host-only; no device call.
+ * No reference counterpart (FlashGen's sampler allocates on the host).
+ */
+size_t fg_sample_workspace_size(int32_t batch, int32_t vocab, int32_t dtype);
 
 /*
  * Local stage of vocabulary-sharded sampling (tensor-parallel LM heads).

@@ -118,4 +118,8 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FLASHGEN_REF", "/root/reference"))
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FLASHGEN_REF")
+    if not ref:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the FlashGen source tree> "
+                 "(or set FLASHGEN_REF)")
+    main(ref)

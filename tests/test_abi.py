@@ -56,7 +56,7 @@ def test_header_compiles_as_cxx(tmp_path):
 
 def test_validation_without_gpu():
     lib = _lib.load()
-    assert lib.fg_version() == 100
+    assert lib.fg_version() == 200
     assert lib.fg_sample(None, None) == _lib.FG_EINVAL
     a = _lib.FgSampleArgs()
     assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # null logits
@@ -67,10 +67,15 @@ def test_validation_without_gpu():
     a.row_stride, a.batch = 8, 0
     assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # no workspace
     a.workspace, a.batch = 256, 1
+    a.workspace_bytes = _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES - 1
+    assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # workspace below the counters
+    a.workspace_bytes = _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES
     a.row_stride = 4
     assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # stride < vocab
     a.row_stride, a.batch = 8, 0
     assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_OK          # empty batch: nothing to do
+    a.batch = (1 << 30) + 1
+    assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_ENOTSUP     # row-queue counter bound
     a.batch, a.hist_ids = 1, 16
     assert lib.fg_sample(ctypes.byref(a), None) == _lib.FG_EINVAL      # ids without offsets
     assert lib.fg_argmax(None, 0, 1, 8, 8, None, None) == _lib.FG_EINVAL
@@ -87,6 +92,17 @@ def test_noalloc_validation_without_gpu():
     a.batch = (1 << 30) + 1
     assert lib.fg_sample_noalloc(ctypes.byref(a), None) == _lib.FG_ESCRATCH
     assert "scratch" in lib.fg_strerror(_lib.FG_ESCRATCH).decode()
+
+
+def test_workspace_size_query_without_gpu():
+    lib = _lib.load()
+    assert lib.fg_sample_workspace_size(1, 256000, _lib.FG_DTYPE_F32) > _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES
+    for B, V in ((1, 256000), (4, 128256), (37, 128256), (1024, 128256), (8, 50257), (1, 7)):
+        n = lib.fg_sample_workspace_size(B, V, _lib.FG_DTYPE_BF16)
+        assert _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES <= n <= _lib.FG_SAMPLE_WORKSPACE_BYTES, (B, V, n)
+    assert lib.fg_sample_workspace_size(1024, 128256, _lib.FG_DTYPE_BF16) == _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES
+    assert lib.fg_sample_workspace_size(1, 8, 9) == 0          # bad dtype
+    assert lib.fg_sample_workspace_size(-1, 8, 0) == 0         # bad batch
 
 
 def test_split_mode_validation_without_gpu():

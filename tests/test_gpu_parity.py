@@ -304,3 +304,25 @@ def test_full_size_all_greedy_equals_argmax(cuda_device):
     np.testing.assert_array_equal(ids, want)
     from flashgen_b200.sampling.sampler import Sampler
     np.testing.assert_array_equal(Sampler.argmax(w.logits.to(dev)).cpu().numpy(), want)
+
+
+def test_host_sampler_back_to_back(cuda_device):
+    """Two HostBatchSampler steps with different parameters and uniforms,
+    enqueued back to back without a sync in between: each step must see its
+    own staging buffers (they are double-buffered), and both results must
+    match the oracle."""
+    from flashgen_b200.sampling.host import HostBatchSampler
+    wa = make_workload(2, batch=64, seed=21)
+    wb = make_workload(3, batch=64, seed=22, vocab=32000)
+    wb.logits = wb.logits.to(torch.float16)
+    hs = HostBatchSampler(64, 32000, torch.float16, max(wa.hist_ids.size, wb.hist_ids.size), cuda_device)
+    outs = []
+    for w in (wa, wb):
+        ids_h = hs.sample(w.logits.pin_memory(), w.params, torch.from_numpy(w.hist_ids).pin_memory(),
+                          torch.from_numpy(w.hist_offsets).pin_memory(), w.uniforms, w.hist_max_len)
+        outs.append(ids_h)
+    torch.cuda.synchronize()
+    for w, ids_h in zip((wa, wb), outs):
+        res = O.sample_rows(w.logits, w.params, w.histories(), w.uniforms)
+        ids = ids_h.numpy()
+        assert ((ids == res.ids) | res.near_u | res.near_p).all(), (w.config, ids[:8], res.ids[:8])

@@ -27,7 +27,8 @@ def _args(w, logits, packed, hist, uni, out, status, workspace):
     a.top_k, a.greedy = packed.top_k.data_ptr(), packed.greedy.data_ptr()
     a.uniforms = uni.data_ptr()
     a.out_ids, a.out_status = out.data_ptr(), status.data_ptr()
-    a.workspace = workspace
+    if workspace is not None:
+        _lib.set_workspace(a, workspace)
     return a
 
 
@@ -50,7 +51,7 @@ def test_noalloc_matches_fg_sample(cuda_device, cfg, batch):
         out_b = torch.full((w.batch,), -7, dtype=torch.int64, device=dev)
         st_a = torch.full((w.batch,), -7, dtype=torch.int32, device=dev)
         st_b = torch.full((w.batch,), -7, dtype=torch.int32, device=dev)
-        a = _args(w, logits, packed, hist, uni, out_a, st_a, ws.data_ptr())
+        a = _args(w, logits, packed, hist, uni, out_a, st_a, ws)
         b = _args(w, logits, packed, hist, uni, out_b, st_b, None)
         assert lib.fg_sample(ctypes.byref(a), stream) == _lib.FG_OK
         assert lib.fg_sample_noalloc(ctypes.byref(b), stream) == _lib.FG_OK
