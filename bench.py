@@ -317,7 +317,8 @@ def main():
     out = torch.empty(B, dtype=torch.int64, device=dev)
     status = torch.empty(B, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    wspace = torch.zeros(_lib.FG_SAMPLE_WORKSPACE_BYTES // 4, dtype=torch.int32, device=dev)
+    need = _lib.workspace_size(B, V, _DTYPES[logits[0].dtype], w.hist_max_len)
+    wspace = torch.zeros((need + 3) // 4, dtype=torch.int32, device=dev)
 
     def make_args(i):
         a = _lib.FgSampleArgs()

@@ -61,7 +61,6 @@ class FgSampleArgs(ctypes.Structure):
     ]
 
 
-FG_SAMPLE_WORKSPACE_BYTES = 262144
 FG_SAMPLE_WORKSPACE_MIN_BYTES = 256
 
 
@@ -89,7 +88,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib = ctypes.CDLL(path)
         lib.fg_sample.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p]
         lib.fg_sample.restype = ctypes.c_int
-        lib.fg_sample_workspace_size.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
+        lib.fg_sample_workspace_size.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
         lib.fg_sample_workspace_size.restype = ctypes.c_size_t
         lib.fg_sample_candidates.argtypes = [ctypes.POINTER(FgSampleArgs), ctypes.c_void_p, ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
@@ -117,6 +116,11 @@ def set_workspace(a: FgSampleArgs, ws) -> None:
     """Point ``a`` at a device workspace tensor and record its size."""
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel() * ws.element_size()
+
+
+def workspace_size(batch: int, vocab: int, dtype: int, hist_max_len: int) -> int:
+    """Workspace bytes of fg_sample's fastest path for this shape."""
+    return int(load().fg_sample_workspace_size(batch, vocab, dtype, max(0, int(hist_max_len))))
 
 
 def check(rc: int, what: str) -> None:

@@ -4,9 +4,12 @@
 
 The library is plain nvcc output (``-shared``, static CUDA runtime) so that it
 has no torch dependency and loads through ctypes, cgo, JNI or pybind11 alike.
+Each kernel lives in its own translation unit; the units compile in parallel
+to objects under ``flashgen_b200/lib/obj`` and link into the one library.
 """
 from __future__ import annotations
 
+import glob
 import os
 import shutil
 import subprocess
@@ -16,18 +19,16 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
+OBJDIR = os.path.join(LIBDIR, "obj")
 LIBNAME = "libflashgen_sampler.so"
 LIBPATH = os.path.join(LIBDIR, LIBNAME)
-SOURCES = [os.path.join(CSRC, "fg_abi.cu")]
-DEPS = SOURCES + [os.path.join(CSRC, f) for f in ("fg_common.cuh", "fg_sample_kernel.cuh", "fg_kernels.cuh")] + [
+SOURCES = [os.path.join(CSRC, f) for f in ("fg_abi.cu", "fg_host.cu", "fg_cluster.cu", "fg_stream.cu")]
+HEADERS = sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))) + [
     os.path.join(ROOT, "include", "flashgen_sampler.h")]
+DEPS = SOURCES + HEADERS
 
-NVCC_FLAGS = [
-    "-gencode", "arch=compute_100a,code=sm_100a",
-    "-lineinfo", "-O3", "-std=c++17",
-    "-Xcompiler", "-fPIC", "-shared",
-    "-Xptxas", "-v",
-]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v"]
 
 
 def nvcc_path() -> str:
@@ -46,14 +47,29 @@ def up_to_date() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIBPATH
-    os.makedirs(LIBDIR, exist_ok=True)
+    os.makedirs(OBJDIR, exist_ok=True)
+    nvcc = nvcc_path()
+    procs = []
+    objs = []
+    for src in SOURCES:
+        obj = os.path.join(OBJDIR, os.path.basename(src).replace(".cu", ".o"))
+        objs.append(obj)
+        cmd = [nvcc, *NVCC_FLAGS, "-c", "-o", obj, src]
+        procs.append((cmd, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    errors = []
+    for cmd, p in procs:
+        out, err = p.communicate()
+        if p.returncode != 0:
+            errors.append(" ".join(cmd) + "\n" + out + err)
+        elif verbose:
+            sys.stderr.write(err)
+    if errors:
+        raise RuntimeError("nvcc failed:\n" + "\n".join(errors))
     tmp = LIBPATH + ".tmp"
-    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", tmp, *SOURCES]
-    res = subprocess.run(cmd, capture_output=True, text=True)
+    link = [nvcc, *ARCH, "-shared", "-o", tmp, *objs]
+    res = subprocess.run(link, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
-    if verbose:
-        sys.stderr.write(res.stderr)
+        raise RuntimeError("link failed:\n" + " ".join(link) + "\n" + res.stdout + res.stderr)
     os.replace(tmp, LIBPATH)
     return LIBPATH
 

@@ -7,64 +7,28 @@
 #include <atomic>
 #include <mutex>
 
+#include "fg_internal.h"
 #include "fg_kernels.cuh"
 
 namespace {
 
-struct DevInfo {
-    int sms = 0;
-    int smem_optin = 0;
-    int smem_per_sm = 0;
-    bool attr_set[3] = {false, false, false};
-    bool ok = false;
-};
-constexpr int kMaxDevices = 64;
-DevInfo g_dev[kMaxDevices];
-std::mutex g_mu;
-
-int device_info(DevInfo** out) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FG_EDEVICE;
-    std::lock_guard<std::mutex> lk(g_mu);
-    DevInfo& d = g_dev[dev];
-    if (!d.ok) {
-        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return FG_EDEVICE;
-        if (cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-            return FG_EDEVICE;
-        if (cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess)
-            return FG_EDEVICE;
-        d.ok = true;
-    }
-    *out = &d;
-    return FG_OK;
-}
-
-int elem_size(int dtype) {
-    switch (dtype) {
-        case FG_DTYPE_F32: return 4;
-        case FG_DTYPE_F16: return 2;
-        case FG_DTYPE_BF16: return 2;
-        default: return 0;
-    }
-}
-
-int bits_for(int64_t v) {  // smallest b >= 1 with v <= 2^b
-    int b = 1;
-    while ((int64_t(1) << b) < v) ++b;
-    return b;
-}
+using fg::host::DevInfo;
+using fg::host::device_info;
+using fg::host::elem_size;
+using fg::host::bits_for;
+using fg::host::g_mu;
 
 template <int DT>
 int launch_sample(const fg::KParams& P, int smem, int grid, cudaStream_t st, DevInfo* d) {
     auto kern = fg::fg_sample_kernel<DT>;
-    if (!d->attr_set[DT]) {
+    if (!d->attr_set[fg::host::K_ROW][DT]) {
         std::lock_guard<std::mutex> lk(g_mu);
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->smem_optin) != cudaSuccess)
             return FG_EDEVICE;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return FG_EDEVICE;
-        d->attr_set[DT] = true;
+        d->attr_set[fg::host::K_ROW][DT] = true;
     }
     kern<<<grid, fg::NTHREADS, smem, st>>>(P);
     return cudaGetLastError() == cudaSuccess ? FG_OK : FG_ELAUNCH;
@@ -142,98 +106,13 @@ int layout_and_launch(fg::KParams& P, int dtype, DevInfo* d, cudaStream_t st, in
     }
 }
 
-// ---------------------------------------------------------------------------
-// Split path for small batches. One CTA streaming a whole row is bound by its
-// own per-tile latency, so a batch that leaves most SMs idle has each row cut
-// into G column shards, sampled by G CTAs in three launches on the stream:
-//   1. shard stage: every shard's candidates after penalties and temperature
-//      (its top-k set, or its top kSplitCand values with the key from which
-//      that set is complete) and its mass partial (max, sum of exp);
-//   2. merge: each row's G candidate sets, in column order, sampled as one row
-//      (temperature 1, no penalties) with the whole row's mass; a row whose
-//      cut or draw falls where the union may be incomplete is marked;
-//   3. fixup: the marked rows (and rows with errors) sampled whole.
-// Scratch lives in the workspace after its counters.
-// ---------------------------------------------------------------------------
-constexpr int kSplitCand = 256;        // candidates per shard (<= 2 * NB)
-constexpr int kSplitMinCols = 4096;    // shard width below which splitting does not pay
-constexpr size_t kSplitScratch0 = 4096;
-// 0 off, 1 automatic, 2 whenever the shapes allow; process-wide, read once per call
-std::atomic<int> g_split_mode{1};
-
-size_t split_bytes(int64_t B, int G) {
-    const int64_t n = B * G;
-    return kSplitScratch0 + (size_t)n * (8 * kSplitCand + 4 + 4 + 4 + 8 + 16) + (size_t)B * 4 + 16 * 8;
-}
-
-int split_shards(const FgSampleArgs* a, int64_t vtot, const DevInfo* d) {
-    const int mode = g_split_mode.load(std::memory_order_relaxed);
-    if (mode == 0 || a->out_probs != nullptr) return 0;
-    if (a->vocab_offset != 0 || vtot != a->vocab) return 0;
-    if (a->batch > 1 && a->row_stride != a->vocab) return 0;
-    for (int G = 32; G >= 4; G >>= 1) {
-        if (a->vocab % G != 0) continue;
-        const int W = a->vocab / G;
-        if (W < 32) continue;
-        if (mode == 1 && (W < kSplitMinCols || (int64_t)a->batch * G > d->sms)) continue;
-        // the caller's buffer must hold the scratch (a smaller one only turns the path off)
-        if (split_bytes(a->batch, G) > (size_t)FG_SAMPLE_WORKSPACE_BYTES) continue;
-        if (split_bytes(a->batch, G) > a->workspace_bytes) continue;
-        return G;
-    }
-    return 0;
-}
-
-int split_launch(const fg::KParams& P0, const FgSampleArgs* a, int G, DevInfo* d, cudaStream_t st) {
-    const int64_t B = a->batch, n = B * G;
-    uint8_t* w = reinterpret_cast<uint8_t*>(a->workspace) + kSplitScratch0;
-    auto take = [&](size_t bytes) { uint8_t* p = w; w += (bytes + 15) & ~size_t(15); return p; };
-    float* cvals = reinterpret_cast<float*>(take(sizeof(float) * n * kSplitCand));
-    int32_t* cids = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * n * kSplitCand));
-    int32_t* ccount = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * n));
-    uint32_t* cthr = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t) * n));
-    int32_t* cstat = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * n));
-    int64_t* cout = reinterpret_cast<int64_t*>(take(sizeof(int64_t) * n));
-    double* cmz = reinterpret_cast<double*>(take(sizeof(double) * 2 * n));
-    int32_t* mstat = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * B));
-
-    // 1. shard stage: launch row r is row r / G, columns [(r % G) * W, ... + W)
-    fg::KParams S = P0;
-    S.batch = (int32_t)n;
-    S.vocab = a->vocab / G;
-    S.row_stride = S.vocab;
-    S.nshard = G;
-    S.cand_vals = cvals; S.cand_ids = cids; S.cand_count = ccount; S.cand_max = kSplitCand;
-    S.cand_thr = cthr; S.cand_mz = cmz;
-    S.out_ids = cout; S.out_status = cstat; S.out_probs = nullptr;
-    S.nwords = (S.vocab + 31) / 32;
-    if (S.pen_possible) S.hu_cap = std::max(1, std::min(a->hist_max_len, S.vocab));
-    int rc = layout_and_launch(S, a->dtype, d, st);
-    if (rc != FG_OK) return rc;
-
-    // 2. merge: row r is the union of its G shard sets (fp32 values)
-    fg::KParams M = P0;
-    M.logits = cvals; M.vocab = G * kSplitCand; M.row_stride = M.vocab;
-    M.vocab_offset = 0; M.vocab_total = M.vocab;
-    M.hist_ids = nullptr; M.hist_offsets = nullptr;
-    M.rep = nullptr; M.pres = nullptr; M.freq = nullptr;
-    M.pen_possible = 0; M.hu_cap = 0;
-    M.nwords = (M.vocab + 31) / 32;
-    M.merge_g = G; M.id_map = cids; M.shard_mz = cmz; M.shard_thr = cthr; M.shard_status = cstat;
-    M.out_status = mstat; M.final_status = a->out_status; M.out_probs = nullptr;
-    rc = layout_and_launch(M, FG_DTYPE_F32, d, st, a->vocab);
-    if (rc != FG_OK) return rc;
-
-    // 3. fixup: the rows the merge left undecided, sampled whole
-    fg::KParams F = P0;
-    F.redo = mstat;
-    return layout_and_launch(F, a->dtype, d, st);
-}
+// Cluster path mode (fg_cluster.cu): 0 off, 1 automatic, 2 always;
+// process-wide, read once per call.
+std::atomic<int> g_cluster_mode{1};
 
 // fg_sample's launch; the candidate outputs are non-null only for
 // fg_sample_candidates.
-int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* cids, int32_t* ccount, int32_t cmax,
-                  bool allow_split) {
+int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* cids, int32_t* ccount, int32_t cmax) {
     if (a == nullptr) return FG_EINVAL;
     const int esz = elem_size(a->dtype);
     if (esz == 0 || a->logits == nullptr || a->batch < 0 || a->vocab < 1) return FG_EINVAL;
@@ -276,8 +155,20 @@ int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* ci
         P.hu_cap = 0;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int G = (cvals == nullptr && allow_split) ? split_shards(a, vtot, d) : 0;
-    if (G > 1) return split_launch(P, a, G, d, st);
+    if (cvals == nullptr) {
+        // sampling: small batches (or every batch in mode 2, and calls that
+        // want kept-set probabilities) with one cluster per row; otherwise the
+        // batch kernel, which hands the rows it cannot decide on chip to the
+        // cluster kernel
+        const int mode = g_cluster_mode.load(std::memory_order_relaxed);
+        int G = fg::host::cluster_size_for(a, d, mode);
+        if (G == 0 && a->out_probs != nullptr) G = std::min(4, std::max(1, fg::host::cluster_size_for(a, d, 2)));
+        if (G > 0) return fg::host::cluster_launch(a, vtot, true, G, P.pen_possible != 0, P.hu_cap, d, st);
+        rc = fg::host::stream_launch(a, vtot, P.pen_possible != 0, P.hu_cap, d, st);
+        if (rc != FG_ENOTSUP) return rc;
+        G = std::max(1, fg::host::cluster_size_for(a, d, 2) >= 8 ? 8 : fg::host::cluster_size_for(a, d, 2));
+        return fg::host::cluster_launch(a, vtot, true, G, P.pen_possible != 0, P.hu_cap, d, st);
+    }
     return layout_and_launch(P, a->dtype, d, st);
 }
 }  // namespace
@@ -285,31 +176,25 @@ int sample_launch(const FgSampleArgs* a, void* stream, float* cvals, int32_t* ci
 extern "C" {
 
 int fg_sample(const FgSampleArgs* a, void* stream) {
-    return sample_launch(a, stream, nullptr, nullptr, nullptr, 0, true);
+    return sample_launch(a, stream, nullptr, nullptr, nullptr, 0);
 }
 
 int fg_sample_set_split(int mode) {
     if (mode < 0 || mode > 2) return FG_EINVAL;
-    g_split_mode.store(mode, std::memory_order_relaxed);
+    g_cluster_mode.store(mode, std::memory_order_relaxed);
     return FG_OK;
 }
 
-size_t fg_sample_workspace_size(int32_t batch, int32_t vocab, int32_t dtype) {
-    if (elem_size(dtype) == 0 || batch < 0 || vocab < 1 || batch > kMaxBatch) return 0;
-    // the largest split scratch any shard count G may use for this shape
-    size_t need = (size_t)FG_SAMPLE_WORKSPACE_MIN_BYTES;
-    for (int G = 32; G >= 4; G >>= 1) {
-        if (vocab % G != 0 || vocab / G < 32) continue;
-        const size_t b = split_bytes(batch, G);
-        if (b <= (size_t)FG_SAMPLE_WORKSPACE_BYTES) need = std::max(need, b);
-    }
-    return need;
+size_t fg_sample_workspace_size(int32_t batch, int32_t vocab, int32_t dtype, int32_t hist_max_len) {
+    if (elem_size(dtype) == 0 || batch < 0 || vocab < 1 || batch > kMaxBatch || hist_max_len < 0) return 0;
+    return std::max((size_t)FG_SAMPLE_WORKSPACE_MIN_BYTES,
+                    fg::host::stream_workspace_bytes(batch, vocab, hist_max_len, hist_max_len > 0));
 }
 
 int fg_sample_candidates(const FgSampleArgs* a, float* vals, int32_t* gids, int32_t* counts, int32_t cand_max,
                          void* stream) {
     if (vals == nullptr || gids == nullptr || counts == nullptr || cand_max < 1) return FG_EINVAL;
-    return sample_launch(a, stream, vals, gids, counts, cand_max, false);
+    return sample_launch(a, stream, vals, gids, counts, cand_max);
 }
 
 // ---------------------------------------------------------------------------
@@ -334,7 +219,7 @@ struct NoAllocSlot {
     unsigned long long ctx_id = 0;   // driver context id the address belongs to (0: none yet)
     void* ptr = nullptr;
 };
-NoAllocSlot g_noalloc[kMaxDevices];
+NoAllocSlot g_noalloc[fg::host::kMaxDevices];
 static_assert(sizeof(fg::Workspace) <= kNoAllocScratchBytes, "static scratch smaller than the row-queue counters");
 
 // Unique id of the current driver context (cuCtxGetCurrent + cuCtxGetId,
@@ -371,7 +256,7 @@ int fg_sample_noalloc(const FgSampleArgs* a, void* stream) {
     if (a == nullptr || a->workspace != nullptr) return FG_EINVAL;
     if (a->batch > kNoAllocMaxBatch) return FG_ESCRATCH;
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FG_EDEVICE;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= fg::host::kMaxDevices) return FG_EDEVICE;
     void* ws = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
@@ -396,8 +281,7 @@ int fg_sample_noalloc(const FgSampleArgs* a, void* stream) {
     FgSampleArgs b = *a;
     b.workspace = ws;
     b.workspace_bytes = kNoAllocScratchBytes;
-    // the fixed scratch holds the row-queue counters only: no split path
-    return sample_launch(&b, stream, nullptr, nullptr, nullptr, 0, false);
+    return sample_launch(&b, stream, nullptr, nullptr, nullptr, 0);
 }
 
 int fg_argmax(const void* logits, int32_t dtype, int32_t batch, int32_t vocab, int64_t row_stride,

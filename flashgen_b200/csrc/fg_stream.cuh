@@ -1,0 +1,1374 @@
+// fg_stream.cuh — the batch path of fg_sample (sm_100a): three kernels per call.
+//
+//   K1 prep_kernel     one CTA per row with penalties: the row's distinct history
+//                      columns in ascending order, with their counts, raw logits
+//                      and penalised values (FlashGen's repetition penalty, plus
+//                      presence and frequency), written to the row's workspace
+//                      block; the best penalised value (greedy rows).
+//   K2 stream_kernel   persistent CTAs, two per SM, each a producer warp and
+//                      NCW consumer warps. The producer takes rows from a global
+//                      queue (rows that sum exp over the whole row first) and
+//                      streams each row's 16-byte-aligned interior HBM -> shared
+//                      memory through a deep ring of 8 KB stages with 1-D bulk
+//                      async copies (cp.async.bulk, completion on mbarriers),
+//                      claiming the next row as soon as the current row's last
+//                      copy is issued. The consumers keep per tile a packed
+//                      NaN-propagating maximum, and by row class the first
+//                      argmax (greedy rows, finished here), an online sum of exp
+//                      over the raw row (top-k off), and a candidate filter
+//                      x >= tau that appends (key, column) of columns outside
+//                      the history (a binary search in the row's sorted history
+//                      list) to a shared buffer. tau starts from the tile-0
+//                      thread maxima and rises with one-pass compactions of the
+//                      buffer. At the row's end the buffer and the row's
+//                      statistics go to the row's workspace block: the next
+//                      row's tiles are already in the ring.
+//   K3 decide_kernel   one small CTA per remaining row: the candidates plus the
+//                      penalised history entries at or above tau, the sum of exp
+//                      corrected for the history columns, then the exact K-th
+//                      largest, top-p cut and draw (integer masses, radix
+//                      selects). A row the candidates cannot decide is handed to
+//                      the cluster kernel (fg_cluster.cuh): out_ids = kDeferredId.
+//
+// Reference: flashgen/sampling/sampler.py:57-169; draw order of
+// csrc/runtime/pipeline.cpp:311-340.
+#pragma once
+
+#include "fg_row.cuh"
+
+namespace fg {
+namespace strm {
+
+constexpr int NCW = 8;                  // consumer warps
+constexpr int NCT = NCW * 32;           // consumer threads
+constexpr int NTH = NCT + 32;           // + producer warp
+constexpr int TILE = 16384;             // ring stage bytes
+constexpr int CPT = TILE / 16 / NCT;    // 16-byte chunks per consumer thread per tile
+constexpr int RQ = 2;                   // row-queue slots
+constexpr int NB = 256;                 // radix bins
+constexpr int BAR = 1;                  // named barrier of the consumer warps
+constexpr uint32_t kSkip = 0x80000000u; // row-queue flag: the row is not streamed
+constexpr int64_t kPendingId = -3;      // out_ids of a row K2 leaves to K3
+
+// Per-row workspace block (16-byte aligned parts):
+//   RowStat, HistHdr, hcol[hu_cap], hraw[hu_cap], hpen[hu_cap], ckey[cap], ccol[cap]
+struct RowStat {
+    double zr;        // sum over the raw row of 2^((x - mraw) * c)
+    float mraw;       // NaN-propagating maximum of the raw row
+    float tau;        // the candidates are complete above tau (penalised, non-history)
+    uint32_t n;       // candidates
+    uint32_t ovf;     // the buffer overflowed: incomplete
+    uint32_t pad[2];
+};
+struct HistHdr {
+    uint32_t nh;      // distinct history columns kept (<= hu_cap)
+    uint32_t flags;   // FG_ROW_BAD_HISTORY / FG_ROW_BAD_PARAM
+    float pbest;      // best penalised history value and its first column
+    uint32_t pcol;
+};
+__host__ __device__ inline int64_t wrow_bytes(int hu_cap, int cap) {
+    return (int64_t)sizeof(RowStat) + (int64_t)sizeof(HistHdr) + 12ll * ((hu_cap + 3) / 4 * 4) + 8ll * cap;
+}
+
+struct Params {
+    const void* logits;
+    int64_t row_stride;
+    int32_t batch, vocab;
+    int64_t vocab_offset, vocab_total;
+    const int32_t* hist_ids;
+    const int64_t* hist_offsets;
+    const float* temperature;
+    const float* top_p;
+    const int32_t* top_k;
+    const float* rep;
+    const float* pres;
+    const float* freq;
+    const uint8_t* greedy;
+    const float* uniforms;
+    int64_t* out_ids;
+    int32_t* out_status;
+    unsigned int* ws;          // [0] queue position, [1] finished CTAs
+    uint8_t* wrow;             // per-row blocks
+    int64_t wrow_bytes;
+    int32_t nstage;
+    int32_t cap;               // candidate buffer entries (shared memory and row block)
+    int32_t k_fast;            // largest top-k decided from the candidates
+    int32_t k_nuc;             // candidate target of rows with top-k off
+    int32_t hu_cap;            // history table entries (0: no penalties in this call)
+    int32_t hcap4;             // hu_cap rounded up to 4
+    int32_t hslots;            // K1: hash slots (power of two >= 2 * hu_cap)
+    int32_t nwords;            // K1: history bitmap words
+    int32_t pen_possible;
+    int32_t mass_shift;
+    int32_t off_ctl, off_bins, off_ckey, off_ccol, off_hcol, off_hpen, off_ring;
+};
+
+// Parts of row r's workspace block.
+__device__ __forceinline__ RowStat* row_stat(const Params& P, int r) {
+    return reinterpret_cast<RowStat*>(P.wrow + (int64_t)r * P.wrow_bytes);
+}
+__device__ __forceinline__ HistHdr* hist_hdr(const Params& P, int r) {
+    return reinterpret_cast<HistHdr*>(P.wrow + (int64_t)r * P.wrow_bytes + sizeof(RowStat));
+}
+__device__ __forceinline__ uint32_t* g_hcol(const Params& P, int r) {
+    return reinterpret_cast<uint32_t*>(P.wrow + (int64_t)r * P.wrow_bytes + sizeof(RowStat) + sizeof(HistHdr));
+}
+__device__ __forceinline__ float* g_hraw(const Params& P, int r) {
+    return reinterpret_cast<float*>(g_hcol(P, r) + P.hcap4);
+}
+__device__ __forceinline__ float* g_hpen(const Params& P, int r) {
+    return reinterpret_cast<float*>(g_hcol(P, r) + 2 * P.hcap4);
+}
+__device__ __forceinline__ uint32_t* g_ckey(const Params& P, int r) { return g_hcol(P, r) + 3 * P.hcap4; }
+__device__ __forceinline__ uint32_t* g_ccol(const Params& P, int r) { return g_ckey(P, r) + P.cap; }
+
+struct SelRes {
+    uint32_t key;
+    uint32_t ok;
+    uint32_t nat;
+    uint32_t pad;
+    unsigned long long before, at;
+};
+
+struct Ctl {
+    uint32_t rowq[RQ];
+    int abort;
+    int status;
+    uint32_t ncand;
+    uint32_t ovf;
+    uint32_t nuniq;
+    uint32_t snap;
+    float tau;
+    uint32_t b32[4];
+    SelRes sel;
+    float redf[NCW];
+    uint32_t red32[NCW];
+    uint32_t red32b[NCW];
+    unsigned long long red64[NCW];
+    double redd[NCW];
+};
+
+extern __shared__ __align__(128) uint8_t ssmem[];
+
+struct Sm {
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* rfull;
+    uint64_t* rempty;
+    Ctl* ctl;
+    uint32_t* bcnt;   // [NB]
+    uint32_t* blo;    // [NB]
+    uint32_t* bhi;    // [NB]
+    uint32_t* ckey;
+    uint32_t* ccol;
+    uint32_t* hcol;   // the row's sorted history columns (K2, K3)
+    float* hpen;      // K3: their penalised values; K1: hash / bitmap area
+    uint8_t* ring;
+};
+__host__ __device__ inline int bar_bytes(int ns) { return 8 * (2 * ns + 2 * RQ); }
+__device__ __forceinline__ Sm carve(const Params& P) {
+    Sm s;
+    s.full = reinterpret_cast<uint64_t*>(ssmem);
+    s.empty = s.full + P.nstage;
+    s.rfull = s.empty + P.nstage;
+    s.rempty = s.rfull + RQ;
+    s.ctl = reinterpret_cast<Ctl*>(ssmem + P.off_ctl);
+    s.bcnt = reinterpret_cast<uint32_t*>(ssmem + P.off_bins);
+    s.blo = s.bcnt + NB;
+    s.bhi = s.blo + NB;
+    s.ckey = reinterpret_cast<uint32_t*>(ssmem + P.off_ckey);
+    s.ccol = reinterpret_cast<uint32_t*>(ssmem + P.off_ccol);
+    s.hcol = reinterpret_cast<uint32_t*>(ssmem + P.off_hcol);
+    s.hpen = reinterpret_cast<float*>(ssmem + P.off_hpen);
+    s.ring = ssmem + P.off_ring;
+    return s;
+}
+
+// ---------------------------------------------------------------------------
+// Consumer-group reductions (named barrier BAR, NCT threads)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void csync() { named_sync(BAR, NCT); }
+
+// ---------------------------------------------------------------------------
+// Consumer-group reductions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float c_max_nan(float v, const Sm& s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmax_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) s.ctl->redf[w] = v;
+    csync();
+    float r = s.ctl->redf[0];
+#pragma unroll
+    for (int i = 1; i < NCW; ++i) r = fmax_nan(r, s.ctl->redf[i]);
+    csync();
+    return r;
+}
+__device__ __forceinline__ uint32_t c_sum_u32(uint32_t v, const Sm& s) {
+    v = __reduce_add_sync(0xffffffffu, v);
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) s.ctl->red32[w] = v;
+    csync();
+    uint32_t r = 0;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) r += s.ctl->red32[i];
+    csync();
+    return r;
+}
+__device__ __forceinline__ void c_minmax_u32(uint32_t& mn, uint32_t& mx, const Sm& s) {
+    mn = __reduce_min_sync(0xffffffffu, mn);
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { s.ctl->red32[w] = mn; s.ctl->red32b[w] = mx; }
+    csync();
+    uint32_t a = s.ctl->red32[0], b = s.ctl->red32b[0];
+#pragma unroll
+    for (int i = 1; i < NCW; ++i) { a = min(a, s.ctl->red32[i]); b = max(b, s.ctl->red32b[i]); }
+    csync();
+    mn = a;
+    mx = b;
+}
+__device__ __forceinline__ unsigned long long c_sum_u64(unsigned long long v, const Sm& s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += shfl_u64(v, (threadIdx.x & 31) ^ o);
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) s.ctl->red64[w] = v;
+    csync();
+    unsigned long long r = 0;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) r += s.ctl->red64[i];
+    csync();
+    return r;
+}
+// Deterministic double sum: fixed shuffle tree, then warps in index order.
+__device__ __forceinline__ double c_sum_f64(double v, const Sm& s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) s.ctl->redd[w] = v;
+    csync();
+    double r = 0.0;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) r += s.ctl->redd[i];
+    csync();
+    return r;
+}
+__device__ __forceinline__ bool arg_better(float v, uint32_t c, float v2, uint32_t c2) {
+    return v > v2 || (v == v2 && c < c2);
+}
+__device__ __forceinline__ void c_argmax(float& v, uint32_t& c, const Sm& s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        const uint32_t c2 = __shfl_xor_sync(0xffffffffu, c, o);
+        if (arg_better(v2, c2, v, c)) { v = v2; c = c2; }
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { s.ctl->redf[w] = v; s.ctl->red32[w] = c; }
+    csync();
+    float bv = s.ctl->redf[0];
+    uint32_t bc = s.ctl->red32[0];
+#pragma unroll
+    for (int i = 1; i < NCW; ++i)
+        if (arg_better(s.ctl->redf[i], s.ctl->red32[i], bv, bc)) { bv = s.ctl->redf[i]; bc = s.ctl->red32[i]; }
+    csync();
+    v = bv;
+    c = bc;
+}
+
+// ---------------------------------------------------------------------------
+// Radix select (descending keys) over weights that every consumer thread
+// yields through enumerate(f): f(valid, key, weight), called the same number
+// of times in every lane of a warp. Finds the key k* with
+//     W(keys > k*) <= target < W(keys >= k*)
+// among keys in [klo, khi]. Exact integer weights (counts when !MASS).
+// ---------------------------------------------------------------------------
+struct Sel {
+    uint32_t key;
+    uint64_t before, at;
+    uint32_t nat;
+    bool ok;
+};
+__device__ __forceinline__ int varying_bits(uint32_t lo, uint32_t hi) {
+    const uint32_t d = lo ^ hi;
+    return d == 0 ? 0 : 32 - __clz(d);
+}
+// Warp 0: the digit of nb (<= NB) bins, scanned in descending order, that
+// holds `rel`.
+template <bool MASS>
+__device__ __forceinline__ void scan_desc(const Sm& s, int nb, uint64_t rel) {
+    const int lane = threadIdx.x & 31;
+    uint64_t v[8];
+    uint64_t lsum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int o = lane * 8 + j;
+        const int d = nb - 1 - o;
+        v[j] = (o < nb) ? (MASS ? (((uint64_t)s.bhi[d] << 32) | s.blo[d]) : (uint64_t)s.bcnt[d]) : 0ull;
+        lsum += v[j];
+    }
+    const uint64_t incl = warp_incl_scan_u64(lsum, lane);
+    const uint64_t excl = incl - lsum;
+    const bool mine = excl <= rel && rel < incl;
+    const uint32_t bal = __ballot_sync(0xffffffffu, mine);
+    SelRes& o = s.ctl->sel;
+    if (bal == 0) {
+        if (lane == 0) o.ok = 0u;
+    } else if (lane == __ffs(bal) - 1) {
+        uint64_t c = excl;
+        int jj = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (jj == j && rel >= c + v[j]) { c += v[j]; jj = j + 1; }
+        if (jj > 7) jj = 7;
+        const int d = nb - 1 - (lane * 8 + jj);
+        o.ok = 1u;
+        o.key = (uint32_t)d;
+        o.before = c;
+        o.nat = s.bcnt[d];
+        o.at = MASS ? (((uint64_t)s.bhi[d] << 32) | s.blo[d]) : (uint64_t)s.bcnt[d];
+    }
+}
+template <bool MASS, class Enum>
+__device__ Sel c_select(const Sm& s, Enum&& enumerate, uint64_t target, uint32_t klo, uint32_t khi) {
+    const int tid = threadIdx.x;
+    Sel out;
+    out.ok = false; out.key = 0u; out.before = 0; out.at = 0; out.nat = 0u;
+    if (klo > khi) return out;
+    int rem = varying_bits(klo, khi);
+    uint32_t pmask = rem >= 32 ? 0u : ~((1u << rem) - 1u);
+    uint32_t prefix = klo & pmask;
+    uint64_t before = 0;
+    if (rem == 0) {
+        // a single key: its weight
+        uint64_t w = 0, n = 0;
+        enumerate([&](bool valid, uint32_t k, uint64_t wt) {
+            if (valid && k == prefix) { ++n; w += MASS ? wt : 1ull; }
+        });
+        const uint64_t W = c_sum_u64(w, s);
+        const uint64_t N = MASS ? c_sum_u64(n, s) : W;
+        out.ok = target < W; out.key = prefix; out.before = 0; out.at = W; out.nat = (uint32_t)N;
+        return out;
+    }
+    while (rem > 0) {
+        const int w = rem < 8 ? rem : 8;
+        const int shift = rem - w;
+        const uint32_t dmask = (1u << w) - 1u;
+        for (int b = tid; b < NB; b += NCT) { s.bcnt[b] = 0u; s.blo[b] = 0u; s.bhi[b] = 0u; }
+        csync();
+        const uint32_t pm = pmask, pf = prefix;
+        enumerate([&](bool valid, uint32_t k, uint64_t wt) {
+            if (!valid || (k & pm) != pf) return;
+            const uint32_t d = (k >> shift) & dmask;
+            atomicAdd(&s.bcnt[d], 1u);
+            if (MASS && wt) {
+                const uint32_t l = (uint32_t)wt;
+                uint32_t h = (uint32_t)(wt >> 32);
+                if (l) {
+                    const uint32_t old = atomicAdd(&s.blo[d], l);
+                    h += (old + l < old) ? 1u : 0u;
+                }
+                if (h) atomicAdd(&s.bhi[d], h);
+            }
+        });
+        csync();
+        if (tid < 32) scan_desc<MASS>(s, 1 << w, target - before);
+        csync();
+        const SelRes r = s.ctl->sel;
+        csync();
+        if (!r.ok) return out;
+        before += r.before;
+        prefix |= r.key << shift;
+        pmask |= dmask << shift;
+        rem = shift;
+        out.at = r.at;
+        out.nat = r.nat;
+    }
+    out.ok = true;
+    out.key = prefix;
+    out.before = before;
+    return out;
+}
+
+// ---------------------------------------------------------------------------
+// Chunk helpers (one 16-byte chunk = VEC elements)
+// ---------------------------------------------------------------------------
+template <int DT>
+__device__ __forceinline__ float elem_at(const uint4& v, int e) {
+    if constexpr (DT == FG_DTYPE_F32) {
+        return __uint_as_float(e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w);
+    } else {
+        const int q = e >> 1;
+        const uint32_t ww = q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w;
+        const uint16_t h = (e & 1) ? (uint16_t)(ww >> 16) : (uint16_t)(ww & 0xffffu);
+        if constexpr (DT == FG_DTYPE_BF16) return __uint_as_float(uint32_t(h) << 16);
+        else return __half2float(__ushort_as_half(h));
+    }
+}
+// NaN-propagating maximum of a chunk (packed pairs for the 16-bit types).
+template <int DT>
+__device__ __forceinline__ float chunk_max(const uint4& v) {
+    if constexpr (DT == FG_DTYPE_F32) {
+        return fmax_nan(fmax_nan(__uint_as_float(v.x), __uint_as_float(v.y)),
+                        fmax_nan(__uint_as_float(v.z), __uint_as_float(v.w)));
+    } else if constexpr (DT == FG_DTYPE_BF16) {
+        const __nv_bfloat162 a = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&v.x),
+                                             *reinterpret_cast<const __nv_bfloat162*>(&v.y));
+        const __nv_bfloat162 b = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&v.z),
+                                             *reinterpret_cast<const __nv_bfloat162*>(&v.w));
+        const __nv_bfloat162 m = __hmax2_nan(a, b);
+        return fmax_nan(__low2float(m), __high2float(m));
+    } else {
+        const __half2 a = __hmax2_nan(*reinterpret_cast<const __half2*>(&v.x), *reinterpret_cast<const __half2*>(&v.y));
+        const __half2 b = __hmax2_nan(*reinterpret_cast<const __half2*>(&v.z), *reinterpret_cast<const __half2*>(&v.w));
+        const __half2 m = __hmax2_nan(a, b);
+        return fmax_nan(__low2float(m), __high2float(m));
+    }
+}
+// Element e of a chunk set to -inf (selects on the four words, so the chunk
+// stays in registers).
+template <int DT>
+__device__ __forceinline__ void elem_mask_inf(uint4& v, int e) {
+    if constexpr (DT == FG_DTYPE_F32) {
+        constexpr uint32_t W = 0xFF800000u;
+        v.x = e == 0 ? W : v.x; v.y = e == 1 ? W : v.y; v.z = e == 2 ? W : v.z; v.w = e == 3 ? W : v.w;
+    } else {
+        constexpr uint32_t W = DT == FG_DTYPE_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
+        const int q = e >> 1;
+        const uint32_t keep = (e & 1) ? 0x0000ffffu : 0xffff0000u;
+        const uint32_t neg = W & ~keep;
+        v.x = q == 0 ? ((v.x & keep) | neg) : v.x;
+        v.y = q == 1 ? ((v.y & keep) | neg) : v.y;
+        v.z = q == 2 ? ((v.z & keep) | neg) : v.z;
+        v.w = q == 3 ? ((v.w & keep) | neg) : v.w;
+    }
+}
+
+// Is column c in the sorted list h[0, n)? (binary search)
+__device__ __forceinline__ bool in_sorted(const uint32_t* h, uint32_t n, uint32_t c) {
+    uint32_t lo = 0, hi = n;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        const uint32_t v = h[mid];
+        if (v == c) return true;
+        if (v < c) lo = mid + 1; else hi = mid;
+    }
+    return false;
+}
+
+// ===========================================================================
+// K1: history of every row with penalties
+// ===========================================================================
+// Distinct history columns with their counts (open-addressed hash), sorted
+// ascending (bitonic sort of the distinct columns only: the work follows the
+// history, not the vocabulary), their raw logits and penalised values.
+template <int DT>
+__global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Params P) {
+    using E = Elem<DT>;
+    const int r = blockIdx.x;
+    const int tid = threadIdx.x;
+    const Sm s = carve(P);
+    HistHdr* hh = hist_hdr(P, r);
+    const bool has_hist = __ldg(P.hist_offsets + r + 1) > __ldg(P.hist_offsets + r);
+    const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms, r,
+                                   has_hist, P.vocab);
+    if (!p.pen) {
+        if (tid == 0) { hh->nh = 0u; hh->flags = 0u; hh->pbest = -INFINITY; hh->pcol = 0xffffffffu; }
+        return;
+    }
+    const Geom g = row_geom<E::SIZE>(P.logits, P.row_stride, P.vocab, r);
+    // shared memory: the count hash, then the distinct columns (sort buffer)
+    uint32_t* hkey = reinterpret_cast<uint32_t*>(ssmem + P.off_ctl + sizeof(Ctl));
+    uint32_t* hcnt = hkey + P.hslots;
+    uint32_t* srt = hcnt + P.hslots;          // hslots / 2 >= hu_cap entries (a power of two)
+    Ctl* ctl = s.ctl;
+    const uint32_t mask = (uint32_t)P.hslots - 1u;
+    for (int i = tid; i < P.hslots; i += NCT) { hkey[i] = kEmptySlot; hcnt[i] = 0u; }
+    if (tid == 0) { ctl->status = 0; ctl->nuniq = 0u; }
+    __syncthreads();
+    const int64_t h0 = __ldg(P.hist_offsets + r), h1 = __ldg(P.hist_offsets + r + 1);
+    uint32_t bad = 0;
+    for (int64_t i = h0 + tid; i < h1; i += NCT) {
+        const int64_t gid = __ldg(P.hist_ids + i);
+        if (gid < 0 || gid >= P.vocab_total) { bad |= FG_ROW_BAD_HISTORY; continue; }
+        const int64_t c = gid - P.vocab_offset;
+        if (c < 0 || c >= P.vocab) continue;
+        const uint32_t cc = (uint32_t)c;
+        uint32_t h = col_hash(cc, mask);
+        bool done = false;
+        for (int probe = 0; probe <= (int)mask; ++probe) {
+            const uint32_t k = atomicCAS(&hkey[h], kEmptySlot, cc);
+            if (k == kEmptySlot) {
+                const uint32_t pos = atomicAdd(&ctl->nuniq, 1u);   // first sighting: a new column
+                if (pos < (uint32_t)P.hu_cap) srt[pos] = cc;
+            }
+            if (k == kEmptySlot || k == cc) { atomicAdd(&hcnt[h], 1u); done = true; break; }
+            h = (h + 1u) & mask;
+        }
+        if (!done) bad |= FG_ROW_BAD_PARAM;   // more distinct ids than hist_max_len allows
+    }
+    if (bad) atomicOr(reinterpret_cast<unsigned int*>(&ctl->status), bad);
+    __syncthreads();
+    const uint32_t total = ctl->nuniq;
+    const uint32_t U = min(total, (uint32_t)P.hu_cap);
+    // bitonic sort of the U distinct columns, padded to a power of two
+    uint32_t N = 1;
+    while (N < U) N <<= 1;
+    for (uint32_t i = U + tid; i < N; i += NCT) srt[i] = 0xffffffffu;
+    __syncthreads();
+    for (uint32_t k = 2; k <= N; k <<= 1) {
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            for (uint32_t t = tid; t < N / 2; t += NCT) {
+                const uint32_t i = ((t & ~(j - 1u)) << 1) | (t & (j - 1u));
+                const uint32_t l = i + j;
+                const uint32_t a = srt[i], b = srt[l];
+                if (((i & k) == 0u) == (a > b)) { srt[i] = b; srt[l] = a; }
+            }
+            __syncthreads();
+        }
+    }
+    uint32_t* hc = g_hcol(P, r);
+    float* hr = g_hraw(P, r);
+    float* hp = g_hpen(P, r);
+    float bv = -INFINITY;
+    uint32_t bc = 0xffffffffu;
+    for (uint32_t i = tid; i < U; i += NCT) {
+        const uint32_t c = srt[i];
+        uint32_t h = col_hash(c, mask), count = 0;
+        for (int probe = 0; probe <= (int)mask; ++probe) {
+            if (hkey[h] == c) { count = hcnt[h]; break; }
+            h = (h + 1u) & mask;
+        }
+        const float raw = E::load(g.row, c);
+        const float pen = penalize(p, raw, count);
+        hc[i] = c; hr[i] = raw; hp[i] = pen;
+        if (arg_better(pen, c, bv, bc)) { bv = pen; bc = c; }
+    }
+    // the best penalised value (first column on ties)
+    const int lane = tid & 31, wid = tid >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t c2 = __shfl_xor_sync(0xffffffffu, bc, o);
+        if (arg_better(v2, c2, bv, bc)) { bv = v2; bc = c2; }
+    }
+    if (lane == 0) { ctl->redf[wid] = bv; ctl->red32b[wid] = bc; }
+    __syncthreads();
+    if (tid == 0) {
+        float v = ctl->redf[0];
+        uint32_t c = ctl->red32b[0];
+        for (int i = 1; i < NCW; ++i)
+            if (arg_better(ctl->redf[i], ctl->red32b[i], v, c)) { v = ctl->redf[i]; c = ctl->red32b[i]; }
+        uint32_t fl = (uint32_t)ctl->status;
+        if (total > (uint32_t)P.hu_cap) fl |= FG_ROW_BAD_PARAM;
+        hh->nh = U;
+        hh->flags = fl;
+        hh->pbest = v;
+        hh->pcol = c;
+    }
+}
+
+// ===========================================================================
+// K2: the stream
+// ===========================================================================
+struct St {
+    float mx;          // NaN-propagating maximum of the raw row
+    float bv;          // greedy: best non-history value and its first column
+    uint32_t bc;
+    float zm, nzc;     // sum of exp: running reference and -(zm * c)
+    float z0, z1;
+    float c;           // log2(e) / T
+    float tau;         // candidate filter (x >= tau)
+    bool cand;         // the buffer is still complete above tau
+};
+
+__device__ __forceinline__ void append(const Params& P, const Sm& s, float x, uint32_t col) {
+    const uint32_t pos = atomicAdd(&s.ctl->ncand, 1u);
+    if (pos < (uint32_t)P.cap) { s.ckey[pos] = fkey(x); s.ccol[pos] = col; } else s.ctl->ovf = 1u;
+}
+
+__device__ __forceinline__ void zadd(St& st, float x) {
+    if (x > st.zm) {
+        const float nn = -(x * st.c);
+        const float f = ex2f_approx(nn - st.nzc);
+        st.z0 *= f; st.z1 *= f;
+        st.zm = x; st.nzc = nn;
+    }
+    st.z0 += ex2f_approx(__fmaf_rn(x, st.c, st.nzc));
+}
+
+// One tile's chunks. CLS: RC_GREEDY, RC_TOPK or RC_NUCLEUS (also for
+// RC_FULL). PEN: the row has history columns: the argmax skips them (a
+// search in the row's sorted list, only when a new maximum appears); the
+// candidates and the sum of exp take the raw row, and K3 swaps the history
+// columns' raw values for their penalised ones.
+template <int DT, int CLS, bool PEN>
+__device__ __forceinline__ void tile_chunks(const Params& P, const Sm& s, const uint4 (&v)[CPT], int nch, int tcol0,
+                                            uint32_t U, St& st) {
+    constexpr int VEC = Elem<DT>::VEC;
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+        const int ch = tid + j * NCT;
+        if (ch >= nch) continue;
+        const int c0 = tcol0 + ch * VEC;
+        const float cm = chunk_max<DT>(v[j]);
+        st.mx = fmax_nan(st.mx, cm);
+        if constexpr (CLS == RC_GREEDY) {
+            if (cm > st.bv) {
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) {
+                    const float x = elem_at<DT>(v[j], e);
+                    if (x > st.bv && !(PEN && in_sorted(s.hcol, U, (uint32_t)(c0 + e)))) {
+                        st.bv = x; st.bc = (uint32_t)(c0 + e);
+                    }
+                }
+            }
+        } else {
+            if constexpr (CLS == RC_NUCLEUS) {
+                if (cm > st.zm) {
+                    const float nn = -(cm * st.c);
+                    const float f = ex2f_approx(nn - st.nzc);
+                    st.z0 *= f; st.z1 *= f;
+                    st.zm = cm; st.nzc = nn;
+                }
+#pragma unroll
+                for (int e = 0; e < VEC; e += 2) {
+                    st.z0 += ex2f_approx(__fmaf_rn(elem_at<DT>(v[j], e), st.c, st.nzc));
+                    st.z1 += ex2f_approx(__fmaf_rn(elem_at<DT>(v[j], e + 1), st.c, st.nzc));
+                }
+            }
+            if (cm >= st.tau) {
+                // every element at or above tau, history columns included (K3
+                // replaces them by their penalised values): one atomic per chunk
+                uint32_t msk = 0u;
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) msk |= (elem_at<DT>(v[j], e) >= st.tau ? 1u : 0u) << e;
+                uint32_t pos = atomicAdd(&s.ctl->ncand, (uint32_t)__popc(msk));
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) {
+                    if (!((msk >> e) & 1u)) continue;
+                    if (pos < (uint32_t)P.cap) {
+                        s.ckey[pos] = fkey(elem_at<DT>(v[j], e));
+                        s.ccol[pos] = (uint32_t)(c0 + e);
+                    } else {
+                        s.ctl->ovf = 1u;
+                    }
+                    ++pos;
+                }
+            }
+        }
+    }
+}
+
+// Starting threshold: a lower bound of the K0-th largest element of the first
+// tile (K0 its share of the row's target, with a margin): a 256-bin histogram
+// of the tile's chunk maxima over their key range gives the lowest key of the
+// bin that holds the K0-th largest maximum; at least K0 chunks, hence K0
+// elements, lie at or above it. -inf when the tile has fewer chunks. A guess
+// for the row: the decision checks that the candidates hold the K-th largest.
+template <int DT>
+__device__ __noinline__ float tile0_tau(const Params& P, int kt, int nch, uint4 v0, uint4 v1, uint4 v2, uint4 v3) {
+    static_assert(CPT == 4, "tile0_tau takes CPT chunks by value");
+    constexpr int VEC = Elem<DT>::VEC;
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    const uint4 v[CPT] = {v0, v1, v2, v3};
+    uint32_t km[CPT];
+    uint32_t kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+        km[j] = 0u;
+        if (tid + j * NCT >= nch) continue;
+        const float cm = chunk_max<DT>(v[j]);
+        if (!(cm == cm)) continue;
+        km[j] = fkey(cm);
+        kmin = min(kmin, km[j]); kmax = max(kmax, km[j]);
+    }
+    const int64_t share = ((int64_t)2 * kt * (int64_t)(nch * VEC) + P.vocab - 1) / P.vocab + 16;
+    const int K0 = (int)min((int64_t)nch, min((int64_t)kt, share));
+    c_minmax_u32(kmin, kmax, s);
+    if (kmin > kmax || K0 < 1) return -INFINITY;
+    const int vb = varying_bits(0u, kmax - kmin);
+    const int shift = vb > 8 ? vb - 8 : 0;
+    for (int b = tid; b < NB; b += NCT) s.bcnt[b] = 0u;
+    csync();
+#pragma unroll
+    for (int j = 0; j < CPT; ++j)
+        if (km[j] != 0u) atomicAdd(&s.bcnt[(km[j] - kmin) >> shift], 1u);
+    csync();
+    if (tid < 32) scan_desc<false>(s, NB, (uint64_t)(K0 - 1));
+    csync();
+    const SelRes rr = s.ctl->sel;
+    csync();
+    if (!rr.ok) return -INFINITY;
+    return funkey(kmin + (rr.key << shift));
+}
+
+// Compaction in one pass: a 256-bin histogram of the buffer's keys over their
+// range; tau rises to the lowest key of the bin that holds the kt-th largest
+// (so at least kt entries stay), closed under equal y. Returns the new count.
+constexpr int CAP_MAX = 4096;
+constexpr int PER_MAX = CAP_MAX / NCT;
+__device__ __noinline__ uint32_t compact(const Params& P, int r, uint32_t n, int kt) {
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms, r,
+                                   false, P.vocab);
+    if (n > (uint32_t)P.cap) n = (uint32_t)P.cap;
+    if (n <= (uint32_t)kt) return n;
+    uint32_t kmin = 0xffffffffu, kmax = 0u;
+    for (uint32_t i = tid; i < n; i += NCT) { const uint32_t k = s.ckey[i]; kmin = min(kmin, k); kmax = max(kmax, k); }
+    c_minmax_u32(kmin, kmax, s);
+    const int vb = varying_bits(0u, kmax - kmin);
+    const int shift = vb > 8 ? vb - 8 : 0;
+    for (int b = tid; b < NB; b += NCT) s.bcnt[b] = 0u;
+    csync();
+    for (uint32_t i = tid; i < n; i += NCT) atomicAdd(&s.bcnt[(s.ckey[i] - kmin) >> shift], 1u);
+    csync();
+    if (tid < 32) scan_desc<false>(s, NB, (uint64_t)(kt - 1));
+    csync();
+    const SelRes rr = s.ctl->sel;
+    csync();
+    if (!rr.ok) return n;
+    const uint32_t klow = kmin + (rr.key << shift);
+    const float tnew = xmin_for_y(p, funkey(klow));
+    if (tid == 0 && tnew > s.ctl->tau) s.ctl->tau = tnew;
+    uint32_t kk[PER_MAX], ii[PER_MAX];
+#pragma unroll
+    for (int j = 0; j < PER_MAX; ++j) {
+        const uint32_t idx = (uint32_t)(j * NCT + tid);
+        kk[j] = idx < n ? s.ckey[idx] : 0u;
+        ii[j] = idx < n ? s.ccol[idx] : 0u;
+    }
+    if (tid == 0) s.ctl->b32[0] = 0u;
+    csync();   // every entry is in registers, tau is published
+    const uint32_t kmin2 = fkey(s.ctl->tau);
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int j = 0; j < PER_MAX; ++j) cnt += ((uint32_t)(j * NCT + tid) < n && kk[j] >= kmin2) ? 1u : 0u;
+    const int lane = tid & 31;
+    const uint32_t incl = warp_incl_scan_u32(cnt, lane);
+    uint32_t base = 0;
+    if (lane == 31) base = atomicAdd(&s.ctl->b32[0], incl);
+    base = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
+#pragma unroll
+    for (int j = 0; j < PER_MAX; ++j)
+        if ((uint32_t)(j * NCT + tid) < n && kk[j] >= kmin2) { s.ckey[base] = kk[j]; s.ccol[base] = ii[j]; ++base; }
+    csync();
+    const uint32_t m = s.ctl->b32[0];
+    csync();
+    return m;
+}
+
+// A row K2 does not stream: top-k above the candidate limit (the cluster
+// kernel samples it) and rows with invalid parameters.
+__device__ __forceinline__ bool row_skipped(const Params& P, int r) {
+    const float T = __ldg(P.temperature + r);
+    const bool g = P.greedy ? (__ldg(P.greedy + r) != 0) : false;
+    if (g || T == 0.0f) return false;
+    const int tk = __ldg(P.top_k + r);
+    const float tp = __ldg(P.top_p + r);
+    const float u = __ldg(P.uniforms + r);
+    if (!(T > 0.0f) || !(tp > 0.0f && tp <= 1.0f) || !(u >= 0.0f && u < 1.0f)) return true;
+    return tk > P.k_fast && tk < P.vocab;
+}
+// Rows that sum exp over the whole row go first.
+__device__ __forceinline__ bool row_heavy(const Params& P, int r) {
+    const float T = __ldg(P.temperature + r);
+    const bool g = P.greedy ? (__ldg(P.greedy + r) != 0) : false;
+    if (g || T == 0.0f) return false;
+    return __ldg(P.top_k + r) <= 0;
+}
+
+template <int DT>
+__device__ void producer(const Params& P) {
+    const Sm s = carve(P);
+    const uint32_t ns = (uint32_t)P.nstage;
+    const unsigned B = (unsigned)P.batch;
+    volatile int* abort = &s.ctl->abort;
+    uint32_t st = 0, ph = 0, k = 0;
+    auto fetch = [&]() -> int {
+        for (;;) {
+            const unsigned v = atomicAdd(&P.ws[0], 1u);
+            if (v >= 2u * B) return -1;
+            const int r = (int)(v % B);
+            if ((v < B) == row_heavy(P, r)) return r;
+        }
+    };
+    int e = fetch();
+    for (;;) {
+        const uint32_t slot = k % RQ, rph = (k / RQ) & 1u;
+        if (!mbar_wait(&s.rempty[slot], rph ^ 1u, abort)) { *abort = 1; return; }
+        const bool skip = e >= 0 && row_skipped(P, e);
+        s.ctl->rowq[slot] = e < 0 ? 0xffffffffu : ((uint32_t)e | (skip ? kSkip : 0u));
+        mbar_arrive(&s.rfull[slot]);
+        ++k;
+        if (e < 0) return;
+        if (!skip) {
+            const Geom g = row_geom<Elem<DT>::SIZE>(P.logits, P.row_stride, P.vocab, e);
+            const int nt = (int)((g.ibytes + TILE - 1) / TILE);
+            for (int t = 0; t < nt; ++t) {
+                if (!mbar_wait(&s.empty[st], ph ^ 1u, abort)) { *abort = 1; return; }
+                const int64_t off = (int64_t)t * TILE;
+                const int64_t left = g.ibytes - off;
+                const uint32_t bytes = (uint32_t)(left < TILE ? left : TILE);
+                mbar_arrive_expect_tx(&s.full[st], bytes);
+                bulk_g2s(s.ring + (int64_t)st * TILE, g.interior + off, bytes, &s.full[st]);
+                if (++st == ns) { st = 0; ph ^= 1u; }
+            }
+        }
+        e = fetch();
+    }
+}
+
+struct Ring { uint32_t st, ph; };
+
+template <int DT, int CLS, bool PEN>
+__device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st_io, int kt, uint32_t U) {
+    using E = Elem<DT>;
+    constexpr int ESZ = E::SIZE;
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const uint32_t ns = (uint32_t)P.nstage;
+    const Geom g = row_geom<ESZ>(P.logits, P.row_stride, P.vocab, r);
+    const int nt = (int)((g.ibytes + TILE - 1) / TILE);
+    St st = st_io;
+    volatile int* abort = &s.ctl->abort;
+    // the buffer may hold up to U history columns with raw values: keep kt
+    // non-history entries above tau by keeping kt + U
+    const int kt2 = min(kt + (int)U, P.cap / 2);
+    uint32_t trig = (uint32_t)min(P.cap * 3 / 4, max(2 * kt2 + 256, 1024));
+    for (int t = 0; t < nt; ++t) {
+        const bool ok = mbar_wait(&s.full[rg.st], rg.ph, abort);
+        if (!ok) *abort = 1;
+        const int64_t left = g.ibytes - (int64_t)t * TILE;
+        const int nch = ok ? (int)((left < TILE ? left : TILE) / 16) : 0;
+        const uint8_t* tile = s.ring + (int64_t)rg.st * TILE;
+        uint4 v[CPT];
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+            const int ch = tid + j * NCT;
+            v[j] = ch < nch ? *reinterpret_cast<const uint4*>(tile + (int64_t)ch * 16) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[rg.st]);
+        if (++rg.st == ns) { rg.st = 0; rg.ph ^= 1u; }
+        const int tcol0 = g.head + t * (TILE / ESZ);
+        if (CLS != RC_GREEDY && t == 0) st.tau = tile0_tau<DT>(P, kt, nch, v[0], v[1], v[2], v[3]);
+        tile_chunks<DT, CLS, PEN>(P, s, v, nch, tcol0, U, st);
+        if (CLS != RC_GREEDY) {
+            const bool check = t < 4 || (t < 16 && (t & 1)) || (t & 3) == 3 || t == nt - 1;
+            if (check) {
+                csync();
+                const uint32_t n = s.ctl->ncand;
+                const bool ovf = s.ctl->ovf != 0u;
+                csync();
+                if (ovf) {
+                    st.cand = false;
+                } else if (st.cand && n > trig) {
+                    const uint32_t m = compact(P, r, n, kt2);
+                    if (tid == 0) s.ctl->ncand = m;
+                    st.tau = s.ctl->tau;
+                    csync();
+                    // ties may keep the count up: compact again only after 512 more
+                    if (m + 512u > trig) trig = min((uint32_t)P.cap - 256u, m + 512u);
+                }
+            }
+        }
+    }
+    st_io = st;
+}
+
+template <int DT, int CLS, bool PEN>
+__device__ __noinline__ void sample_row_cls(const Params& P, int r, Ring& rg, uint32_t U) {
+    using E = Elem<DT>;
+    constexpr int ESZ = E::SIZE;
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms, r,
+                                   PEN, P.vocab);
+    const Geom g = row_geom<ESZ>(P.logits, P.row_stride, P.vocab, r);
+    const int kt = CLS == RC_TOPK ? p.K : P.k_nuc;
+    St st;
+    st.mx = -INFINITY; st.bv = -INFINITY; st.bc = 0xffffffffu;
+    st.c = p.temp_on ? __fdiv_rn(kL2E, p.T) : kL2E;
+    st.zm = -1e30f; st.nzc = -(st.zm * st.c); st.z0 = 0.0f; st.z1 = 0.0f;
+    st.tau = -INFINITY; st.cand = true;
+    stream_row<DT, CLS, PEN>(P, r, rg, st, kt, U);
+    // the ragged head / tail (fewer than VEC each)
+    {
+        const int nh = g.head, ntl = P.vocab - g.tail0;
+        if (tid < nh + ntl) {
+            const int c = tid < nh ? tid : g.tail0 + (tid - nh);
+            const float x = E::load(g.row, c);
+            const bool hist = CLS == RC_GREEDY && PEN && in_sorted(s.hcol, U, (uint32_t)c);
+            st.mx = fmax_nan(st.mx, x);
+            if (CLS == RC_GREEDY) {
+                if (!hist && arg_better(x, (uint32_t)c, st.bv, st.bc)) { st.bv = x; st.bc = (uint32_t)c; }
+            } else {
+                if (CLS == RC_NUCLEUS) zadd(st, x);
+                if (st.cand && x >= st.tau) append(P, s, x, (uint32_t)c);
+            }
+        }
+    }
+    csync();
+    const bool ovf = s.ctl->ovf != 0u;
+    const uint32_t n = min(s.ctl->ncand, (uint32_t)P.cap);
+    const bool aborted = s.ctl->abort != 0;
+    csync();
+    const float M = c_max_nan(st.mx, s);
+    if (CLS == RC_GREEDY) {
+        float bv = st.bv;
+        uint32_t bc = st.bc;
+        c_argmax(bv, bc, s);
+        if (tid == 0) {
+            int status = p.bad | FG_ROW_GREEDY;
+            int64_t out = -1;
+            if (PEN) {
+                const HistHdr* hh = hist_hdr(P, r);
+                status |= (int)hh->flags;
+                if (arg_better(hh->pbest, hh->pcol, bv, bc)) { bv = hh->pbest; bc = hh->pcol; }
+            }
+            bool defer = false;
+            if (aborted) status |= FG_ROW_TIMEOUT;
+            else if (status & (FG_ROW_BAD_PARAM | FG_ROW_BAD_UNIFORM)) out = -1;
+            else if (M != M) defer = true;            // the first NaN: the cluster kernel finds it
+            else out = (M == -INFINITY) ? 0 : (int64_t)bc;
+            if (defer) {
+                P.out_ids[r] = kDeferredId;
+            } else {
+                P.out_ids[r] = out >= 0 ? out + P.vocab_offset : -1;
+                if (P.out_status) P.out_status[r] = status;
+            }
+        }
+    } else {
+        // the candidates and statistics go to the row's block; K3 decides
+        double zc = 0.0;
+        if (CLS == RC_NUCLEUS && M == M && M > -INFINITY && M < INFINITY) {
+            const double zs = (double)st.z0 + (double)st.z1;
+            if (zs > 0.0) zc = zs * exp2(-(double)st.nzc - (double)M * (double)st.c);
+        }
+        if (CLS == RC_NUCLEUS) zc = c_sum_f64(zc, s);
+        uint32_t* gk = g_ckey(P, r);
+        uint32_t* gc = g_ccol(P, r);
+        for (uint32_t i = tid; i < n; i += NCT) { gk[i] = s.ckey[i]; gc[i] = s.ccol[i]; }
+        if (tid == 0) {
+            RowStat* rs = row_stat(P, r);
+            rs->zr = zc;
+            rs->mraw = M;
+            rs->tau = st.tau;
+            rs->n = n;
+            rs->ovf = (ovf || !st.cand || aborted) ? 1u : 0u;
+            if (aborted) {
+                P.out_ids[r] = -1;
+                if (P.out_status) P.out_status[r] = FG_ROW_TIMEOUT;
+            } else {
+                P.out_ids[r] = kPendingId;
+            }
+        }
+    }
+    csync();
+}
+
+template <int DT>
+__device__ void consumer(const Params& P) {
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    Ring rg{0u, 0u};
+    volatile int* abort = &s.ctl->abort;
+    for (uint32_t k = 0;; ++k) {
+        const uint32_t slot = k % RQ, ph = (k / RQ) & 1u;
+        if (tid == 0) {
+            const bool ok = mbar_wait(&s.rfull[slot], ph, abort);
+            s.ctl->snap = ok ? s.ctl->rowq[slot] : 0xfffffffeu;
+            s.ctl->b32[3] = ok ? k + 1 : k;   // next slot to read after an abort
+        }
+        csync();
+        const uint32_t q = s.ctl->snap;
+        csync();
+        if (q == 0xfffffffeu) break;                       // abort
+        if (tid == 0) mbar_arrive(&s.rempty[slot]);
+        if (q == 0xffffffffu) break;                       // no rows left
+        const int r = (int)(q & ~kSkip);
+        const bool has_hist = P.pen_possible && (__ldg(P.hist_offsets + r + 1) > __ldg(P.hist_offsets + r));
+        const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms,
+                                       r, has_hist, P.vocab);
+        if (q & kSkip) {
+            if (tid == 0) {
+                if (p.bad) {
+                    P.out_ids[r] = -1;
+                    if (P.out_status) P.out_status[r] = p.bad;
+                } else {
+                    P.out_ids[r] = kDeferredId;
+                }
+            }
+            continue;
+        }
+        if (tid == 0) { s.ctl->ncand = 0u; s.ctl->ovf = 0u; s.ctl->tau = -INFINITY; }
+        uint32_t U = 0;
+        if (p.pen) {
+            // the row's history size from K1, and for greedy rows its sorted columns
+            U = min(hist_hdr(P, r)->nh, (uint32_t)P.hu_cap);
+            if (p.cls == RC_GREEDY) {
+                const uint32_t* hc = g_hcol(P, r);
+                for (uint32_t i = tid; i < U; i += NCT) s.hcol[i] = hc[i];
+            }
+        }
+        csync();
+        if (p.pen) {
+            if (p.cls == RC_GREEDY) sample_row_cls<DT, RC_GREEDY, true>(P, r, rg, U);
+            else if (p.cls == RC_TOPK) sample_row_cls<DT, RC_TOPK, true>(P, r, rg, U);
+            else sample_row_cls<DT, RC_NUCLEUS, true>(P, r, rg, U);
+        } else {
+            if (p.cls == RC_GREEDY) sample_row_cls<DT, RC_GREEDY, false>(P, r, rg, 0u);
+            else if (p.cls == RC_TOPK) sample_row_cls<DT, RC_TOPK, false>(P, r, rg, 0u);
+            else sample_row_cls<DT, RC_NUCLEUS, false>(P, r, rg, 0u);
+        }
+        if (*abort) break;
+    }
+    if (tid == 0 && *abort) {
+        // rows published to this CTA and not sampled, then every unclaimed
+        // row, are reported as timed out (bounded waits: the producer has
+        // stopped publishing)
+        for (uint32_t k = s.ctl->b32[3];; ++k) {
+            const uint32_t slot = k % RQ, ph = (k / RQ) & 1u;
+            if (!mbar_wait_for(&s.rfull[slot], ph, 10000000ull)) break;
+            const uint32_t q = s.ctl->rowq[slot];
+            mbar_arrive(&s.rempty[slot]);
+            if (q == 0xffffffffu) break;
+            const int rr = (int)(q & ~kSkip);
+            P.out_ids[rr] = -1;
+            if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT;
+        }
+        for (;;) {
+            const unsigned v = atomicAdd(&P.ws[0], 1u);
+            if (v >= 2u * (unsigned)P.batch) break;
+            const int rr = (int)(v % (unsigned)P.batch);
+            if ((v < (unsigned)P.batch) != row_heavy(P, rr)) continue;
+            P.out_ids[rr] = -1;
+            if (P.out_status) P.out_status[rr] = FG_ROW_TIMEOUT;
+        }
+    }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(NTH, 2) stream_kernel(const __grid_constant__ Params P) {
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int i = 0; i < P.nstage; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], NCW); }
+        for (int i = 0; i < RQ; ++i) { mbar_init(&s.rfull[i], 1); mbar_init(&s.rempty[i], 1); }
+        s.ctl->abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid >= NCT) {
+        if (tid == NCT) producer<DT>(P);
+        return;
+    }
+    consumer<DT>(P);
+    csync();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(&P.ws[1], 1u) == gridDim.x - 1) {
+            P.ws[0] = 0u;
+            P.ws[1] = 0u;
+            __threadfence();
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Finish of a row decided in the candidate buffer. Entries [0, n): x-keys
+// and columns; the buffer holds every element with x >= tau. Returns false
+// when the row cannot be decided there (the caller defers it).
+// ---------------------------------------------------------------------------
+struct Fin {
+    int64_t id;
+    int status;
+    bool defer;
+};
+__device__ __noinline__ Fin finish_sampling(const Params& P, int r, uint32_t n, float M, double Zd, float zmax) {
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    const bool has_hist = P.pen_possible && (__ldg(P.hist_offsets + r + 1) > __ldg(P.hist_offsets + r));
+    const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms, r,
+                                   has_hist, P.vocab);
+    Fin fo;
+    fo.id = -1; fo.status = 0; fo.defer = false;
+    const float scale = __uint_as_float((uint32_t)(127 + P.mass_shift) << 23);
+    const float My = ydiv(p, M);
+    const uint32_t ktau = fkey(s.ctl->tau);
+    if (n > (uint32_t)P.cap) n = (uint32_t)P.cap;
+    // C: entries at or above tau, as y-keys; others get key 0 (never selected)
+    uint32_t nabove = 0, ylo = 0xffffffffu, yhi = 0u;
+    for (uint32_t i = tid; i < n; i += NCT) {
+        const uint32_t k = s.ckey[i];
+        uint32_t yk = 0u;
+        if (k >= ktau) {
+            yk = fkey(ydiv(p, funkey(k)));
+            ++nabove;
+            ylo = min(ylo, yk); yhi = max(yhi, yk);
+        }
+        s.ckey[i] = yk;
+    }
+    nabove = c_sum_u32(nabove, s);
+    c_minmax_u32(ylo, yhi, s);
+    auto qm = [&](uint32_t yk) -> uint64_t { return qmass(funkey(yk), My, scale); };
+    // ---- top-k threshold ----
+    uint32_t ykK = 1u;   // every valid entry (keys >= 1)
+    if (p.cls == RC_TOPK) {
+        if (nabove < (uint32_t)p.K) { fo.defer = true; return fo; }
+        const Sel so = c_select<false>(s, [&](auto&& f) {
+            for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+                const uint32_t i = i0 + tid;
+                const uint32_t yk = i < n ? s.ckey[i] : 0u;
+                f(i < n && yk != 0u, yk, 1ull);
+            }
+        }, (uint64_t)(p.K - 1), ylo, yhi);
+        if (!so.ok) { fo.defer = true; return fo; }
+        ykK = so.key;
+    }
+    // ---- masses of the kept part of C ----
+    uint64_t loc = 0;
+    for (uint32_t i = tid; i < n; i += NCT) {
+        const uint32_t yk = s.ckey[i];
+        if (yk != 0u && yk >= ykK) loc += qm(yk);
+    }
+    const uint64_t AC = c_sum_u64(loc, s);
+    auto kept = [&](uint32_t yk) { return yk != 0u && yk >= ykK; };
+    const uint32_t klo = max(ylo, ykK);
+    // ---- total mass and the cut ----
+    uint64_t Qf = 0;
+    bool cut = false;
+    uint32_t tstar = 0u;
+    uint64_t before_t = 0, qt = 0;
+    if (p.cls == RC_TOPK) {
+        if (p.use_p) {
+            const uint64_t Pt = (uint64_t)floor((double)p.top_p * (double)AC);
+            const Sel so = c_select<true>(s, [&](auto&& f) {
+                for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+                    const uint32_t i = i0 + tid;
+                    const uint32_t yk = i < n ? s.ckey[i] : 0u;
+                    const bool v = i < n && kept(yk);
+                    f(v, yk, v ? qm(yk) : 0ull);
+                }
+            }, Pt, klo, yhi);
+            if (!so.ok) { fo.defer = true; return fo; }
+            cut = true; tstar = so.key; before_t = so.before;
+            qt = so.nat ? so.at / so.nat : 0;
+            uint64_t m = so.nat;
+            if (qt > 0) { const uint64_t mm = (Pt - so.before) / qt + 1; if (mm < m) m = mm; }
+            Qf = so.before + m * qt;
+        } else {
+            Qf = AC;
+        }
+    } else {
+        // top-k off: the row's total mass from the online sum of exp
+        const double Zq = Zd * exp((double)zmax / (double)p.T - (double)My) * (double)scale;
+        if (p.use_p) {
+            const uint64_t Pt = (uint64_t)floor((double)p.top_p * Zq);
+            if (Pt >= AC) { fo.defer = true; return fo; }   // the cut lies below the buffer
+            const Sel so = c_select<true>(s, [&](auto&& f) {
+                for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+                    const uint32_t i = i0 + tid;
+                    const uint32_t yk = i < n ? s.ckey[i] : 0u;
+                    const bool v = i < n && kept(yk);
+                    f(v, yk, v ? qm(yk) : 0ull);
+                }
+            }, Pt, klo, yhi);
+            if (!so.ok) { fo.defer = true; return fo; }
+            cut = true; tstar = so.key; before_t = so.before;
+            qt = so.nat ? so.at / so.nat : 0;
+            uint64_t m = so.nat;
+            if (qt > 0) { const uint64_t mm = (Pt - so.before) / qt + 1; if (mm < m) m = mm; }
+            Qf = so.before + m * qt;
+        } else {
+            Qf = (uint64_t)Zq;
+            const uint64_t Dt0 = (uint64_t)floor((double)p.u * (double)Qf);
+            if (Dt0 >= AC) { fo.defer = true; return fo; }   // the draw lies below the buffer
+        }
+    }
+    if (Qf == 0) { fo.defer = true; return fo; }
+    // ---- the draw ----
+    uint64_t Dt = (uint64_t)floor((double)p.u * (double)Qf);
+    if (Dt >= Qf) Dt = Qf - 1;
+    uint32_t dkey;
+    uint64_t dj;
+    if (cut && Dt >= before_t) {
+        dkey = tstar;
+        dj = qt ? (Dt - before_t) / qt : 0;
+    } else {
+        const uint32_t ts = cut ? tstar : 0u;
+        const Sel so = c_select<true>(s, [&](auto&& f) {
+            for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+                const uint32_t i = i0 + tid;
+                const uint32_t yk = i < n ? s.ckey[i] : 0u;
+                const bool v = i < n && kept(yk) && (!cut || yk > ts);
+                f(v, yk, v ? qm(yk) : 0ull);
+            }
+        }, Dt, klo, yhi);
+        if (!so.ok) { fo.defer = true; return fo; }
+        dkey = so.key;
+        const uint64_t qd = so.nat ? so.at / so.nat : 0;
+        dj = qd ? (Dt - so.before) / qd : 0;
+    }
+    // ---- dj-th column (ascending) among the entries at dkey: select on ~column ----
+    uint32_t cmin = 0xffffffffu, cmax = 0u;
+    for (uint32_t i = tid; i < n; i += NCT)
+        if (s.ckey[i] == dkey) { const uint32_t kc = ~s.ccol[i]; cmin = min(cmin, kc); cmax = max(cmax, kc); }
+    c_minmax_u32(cmin, cmax, s);
+    // descending ~column = ascending column; dj-th from the smallest column is
+    // (count - 1 - dj)-th ... counted from the largest ~column
+    const Sel sc = c_select<false>(s, [&](auto&& f) {
+        for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+            const uint32_t i = i0 + tid;
+            const bool v = i < n && s.ckey[i] == dkey;
+            f(v, v ? ~s.ccol[i] : 0u, 1ull);
+        }
+    }, dj, cmin, cmax);
+    if (!sc.ok) { fo.defer = true; return fo; }
+    fo.id = (int64_t)(~sc.key);
+    return fo;
+}
+
+
+// ===========================================================================
+// K3: decide the rows K2 left (out_ids == kPendingId)
+// ===========================================================================
+template <int DT>
+__global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Params P) {
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    for (int r = blockIdx.x; r < P.batch; r += gridDim.x) {
+        if (__ldcg(P.out_ids + r) != kPendingId) continue;
+        const bool has_hist = P.pen_possible && (__ldg(P.hist_offsets + r + 1) > __ldg(P.hist_offsets + r));
+        const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms,
+                                       r, has_hist, P.vocab);
+        const RowStat rs = *row_stat(P, r);
+        const float scale = __uint_as_float((uint32_t)(127 + P.mass_shift) << 23);
+        (void)scale;
+        int status = p.bad;
+        uint32_t U = 0;
+        if (p.pen) {
+            const HistHdr* hh = hist_hdr(P, r);
+            status |= (int)hh->flags;
+            U = min(hh->nh, (uint32_t)P.hu_cap);
+        }
+        bool defer = rs.ovf != 0u;
+        int64_t out = -1;
+        const float Mraw = rs.mraw;
+        if (status & (FG_ROW_BAD_PARAM | FG_ROW_BAD_UNIFORM)) {
+            defer = false;
+        } else if (Mraw != Mraw) {
+            status |= FG_ROW_NAN; defer = false;
+        } else if (Mraw == INFINITY) {
+            status |= FG_ROW_POS_INF; defer = false;
+        } else if (Mraw == -INFINITY) {
+            status |= FG_ROW_ALL_MASKED; defer = false;
+        } else if (!defer) {
+            // the decision set: the candidates (non-history, raw = final) and the
+            // history entries at or above tau with their penalised values
+            const float tau = rs.tau;
+            uint32_t n = min(rs.n, (uint32_t)P.cap);
+            const uint32_t* gk = g_ckey(P, r);
+            const uint32_t* gc = g_ccol(P, r);
+            if (p.pen) {
+                // the row's sorted history columns, then the candidates without them
+                const uint32_t* hcg = g_hcol(P, r);
+                for (uint32_t i = tid; i < U; i += NCT) s.hcol[i] = hcg[i];
+                if (tid == 0) s.ctl->ncand = 0u;
+                csync();
+                for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+                    const uint32_t i = i0 + tid;
+                    const bool keep = i < n && !in_sorted(s.hcol, U, gc[i]);
+                    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+                    uint32_t base = 0;
+                    if ((tid & 31) == 0 && bal) base = atomicAdd(&s.ctl->ncand, (uint32_t)__popc(bal));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (keep) {
+                        const uint32_t pos = base + (uint32_t)__popc(bal & ((1u << (tid & 31)) - 1u));
+                        s.ckey[pos] = gk[i];
+                        s.ccol[pos] = gc[i];
+                    }
+                }
+                csync();
+                n = s.ctl->ncand;
+                csync();
+            } else {
+                for (uint32_t i = tid; i < n; i += NCT) { s.ckey[i] = gk[i]; s.ccol[i] = gc[i]; }
+            }
+            if (tid == 0) { s.ctl->ncand = n; s.ctl->tau = tau; s.ctl->ovf = 0u; }
+            csync();
+            double hcorr = 0.0, hraw = 0.0;
+            float hmax = -INFINITY;
+            if (p.pen) {
+                const uint32_t* hc = g_hcol(P, r);
+                const float* hr = g_hraw(P, r);
+                const float* hp = g_hpen(P, r);
+                const double c = (double)(p.temp_on ? __fdiv_rn(kL2E, p.T) : kL2E);
+                for (uint32_t i = tid; i < U; i += NCT) {
+                    const float pen = hp[i];
+                    hmax = fmax_nan(hmax, pen);
+                    if (pen >= tau) append(P, s, pen, hc[i]);
+                    if (p.cls != RC_TOPK) {
+                        hraw += exp2(((double)hr[i] - (double)Mraw) * c);
+                        hcorr += exp2(((double)pen - (double)Mraw) * c);
+                    }
+                }
+            }
+            hmax = c_max_nan(hmax, s);
+            csync();
+            n = s.ctl->ncand;
+            if (s.ctl->ovf || n > (uint32_t)P.cap) defer = true;
+            csync();
+            if (!defer) {
+                // the row's maximum after penalties: every value at or above tau is
+                // in the set, and the raw maximum of the non-history columns is
+                // one of them unless the set is empty
+                float cmax = -INFINITY;
+                for (uint32_t i = tid; i < n; i += NCT) cmax = fmaxf(cmax, funkey(s.ckey[i]));
+                cmax = c_max_nan(cmax, s);
+                const float M = fmax_nan(cmax, hmax);
+                if (n == 0 || !(M >= tau) || M == INFINITY || M != M) {
+                    defer = true;
+                } else {
+                    double Zd = 0.0;
+                    if (p.cls != RC_TOPK) {
+                        const double hr_t = c_sum_f64(hraw, s);
+                        const double hc_t = c_sum_f64(hcorr, s);
+                        // the raw row's sum without the history columns' raw terms,
+                        // with their penalised terms; relative to M
+                        const double zr = rs.zr;
+                        if (hr_t > 0.5 * zr) {
+                            defer = true;   // most of the raw mass sat on history columns
+                        } else {
+                            const double c = (double)(p.temp_on ? __fdiv_rn(kL2E, p.T) : kL2E);
+                            Zd = (zr - hr_t + hc_t) * exp2(((double)Mraw - (double)M) * c);
+                        }
+                    }
+                    if (!defer) {
+                        const Fin fo = finish_sampling(P, r, n, M, Zd, M);
+                        if (fo.defer) defer = true;
+                        else out = fo.id;
+                    }
+                }
+            }
+        }
+        if (tid == 0) {
+            if (defer) {
+                P.out_ids[r] = kDeferredId;
+            } else {
+                P.out_ids[r] = out >= 0 ? out + P.vocab_offset : -1;
+                if (out < 0 && !(status & FG_ROW_ERROR_MASK)) status |= FG_ROW_ALL_MASKED;
+                if (P.out_status) P.out_status[r] = status;
+            }
+        }
+        csync();
+    }
+}
+
+}  // namespace strm
+}  // namespace fg

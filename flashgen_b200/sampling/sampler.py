@@ -88,13 +88,15 @@ class PackedParams:
 _WORKSPACES = {}
 
 
-def workspace_for(device: torch.device, stream: torch.cuda.Stream) -> torch.Tensor:
-    """The zero-initialised fg_sample workspace of (device, stream). Calls on one
+def workspace_for(device: torch.device, stream: torch.cuda.Stream, nbytes: int = 0) -> torch.Tensor:
+    """The zero-initialised fg_sample workspace of (device, stream), at least
+    `nbytes` long (it grows, zeroed, when a call needs more). Calls on one
     stream are serialised by the stream, so they can share it."""
     key = (device.index, stream.cuda_stream)
     ws = _WORKSPACES.get(key)
-    if ws is None:
-        ws = torch.zeros(_lib.FG_SAMPLE_WORKSPACE_BYTES // 4, dtype=torch.int32, device=device)
+    need = max(int(nbytes), _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES)
+    if ws is None or ws.numel() * 4 < need:
+        ws = torch.zeros((need + 3) // 4, dtype=torch.int32, device=device)
         _WORKSPACES[key] = ws
     return ws
 
@@ -130,7 +132,8 @@ def fused_sample(logits: torch.Tensor, packed: PackedParams, uniforms: torch.Ten
     a.out_probs = _ptr(probs)
     st = stream if stream is not None else torch.cuda.current_stream(logits.device)
     if workspace is None:
-        workspace = workspace_for(logits.device, st)
+        need = _lib.workspace_size(B, V, a.dtype, a.hist_max_len if hist is not None else 0)
+        workspace = workspace_for(logits.device, st, need)
     _lib.set_workspace(a, workspace)
     with torch.cuda.device(logits.device):
         _lib.check(lib.fg_sample(a, st.cuda_stream), "fg_sample")

@@ -132,18 +132,16 @@ typedef struct FgSampleArgs {
  * Workspace: rows are handed to the GPU's persistent CTAs through counters in
  * the first FG_SAMPLE_WORKSPACE_MIN_BYTES of this device buffer. The caller
  * zeroes the buffer once (cudaMemset) before its first use; every fg_sample
- * call leaves the counters zero again. Bytes beyond the counters are scratch
- * for small batches, whose rows fg_sample cuts into column shards sampled by
- * several CTAs (see fg_sample_set_split): that path runs only when
- * workspace_bytes covers its scratch, so a smaller buffer is always safe and
- * only gives up that speed-up. fg_sample_workspace_size(batch, vocab, dtype)
- * gives the size that lets every path run; FG_SAMPLE_WORKSPACE_BYTES is an
- * upper bound of it for any shape. workspace_bytes below
- * FG_SAMPLE_WORKSPACE_MIN_BYTES returns FG_EINVAL. Calls that may run
- * concurrently on the GPU (different streams) need separate workspaces.
+ * call leaves the counters zero again. Bytes beyond the counters hold, for
+ * large batches, a block per row written and read within the call (history
+ * lists and candidate sets of the batch kernels): that path runs only when
+ * workspace_bytes covers fg_sample_workspace_size(batch, vocab, dtype,
+ * hist_max_len), so a smaller buffer is always safe and only gives up that
+ * path. workspace_bytes below FG_SAMPLE_WORKSPACE_MIN_BYTES returns
+ * FG_EINVAL. Calls that may run concurrently on the GPU (different streams)
+ * need separate workspaces.
  */
 #define FG_SAMPLE_WORKSPACE_MIN_BYTES 256
-#define FG_SAMPLE_WORKSPACE_BYTES 262144
 
 /*
  * Batched fused sampling (one decode step). Replaces Sampler.sample
@@ -154,12 +152,16 @@ typedef struct FgSampleArgs {
 int fg_sample(const FgSampleArgs* args, void* stream);
 
 /*
- * Bytes of workspace with which fg_sample may use every path for a batch of
- * this shape (FG_SAMPLE_WORKSPACE_MIN_BYTES when only the counters are
- * needed); 0 for an invalid shape or dtype. Host-only; no device call.
+ * Bytes of workspace with which fg_sample takes its fastest path for a batch
+ * of this shape: the batch kernels keep a block per row (the row's history
+ * list and candidates) after the counters. hist_max_len as in FgSampleArgs
+ * (0 without history). A smaller workspace (at least
+ * FG_SAMPLE_WORKSPACE_MIN_BYTES) is still valid: fg_sample then samples
+ * every row with the cluster kernel, which needs only the counters.
+ * 0 for an invalid shape or dtype. Host-only; no device call.
  * No reference counterpart (FlashGen's sampler allocates on the host).
  */
-size_t fg_sample_workspace_size(int32_t batch, int32_t vocab, int32_t dtype);
+size_t fg_sample_workspace_size(int32_t batch, int32_t vocab, int32_t dtype, int32_t hist_max_len);
 
 /*
  * Local stage of vocabulary-sharded sampling (tensor-parallel LM heads).

@@ -96,13 +96,17 @@ def test_noalloc_validation_without_gpu():
 
 def test_workspace_size_query_without_gpu():
     lib = _lib.load()
-    assert lib.fg_sample_workspace_size(1, 256000, _lib.FG_DTYPE_F32) > _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES
-    for B, V in ((1, 256000), (4, 128256), (37, 128256), (1024, 128256), (8, 50257), (1, 7)):
-        n = lib.fg_sample_workspace_size(B, V, _lib.FG_DTYPE_BF16)
-        assert _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES <= n <= _lib.FG_SAMPLE_WORKSPACE_BYTES, (B, V, n)
-    assert lib.fg_sample_workspace_size(1024, 128256, _lib.FG_DTYPE_BF16) == _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES
-    assert lib.fg_sample_workspace_size(1, 8, 9) == 0          # bad dtype
-    assert lib.fg_sample_workspace_size(-1, 8, 0) == 0         # bad batch
+    # the batch path keeps a block per row; the size grows with batch and history
+    small = _lib.workspace_size(1024, 128256, _lib.FG_DTYPE_BF16, 0)
+    big = _lib.workspace_size(1024, 128256, _lib.FG_DTYPE_BF16, 1024)
+    assert _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES < small < big
+    assert _lib.workspace_size(2048, 128256, _lib.FG_DTYPE_BF16, 1024) > big
+    for B, V in ((1, 256000), (4, 128256), (37, 128256), (8, 50257), (1, 7)):
+        for dt in (_lib.FG_DTYPE_F32, _lib.FG_DTYPE_F16, _lib.FG_DTYPE_BF16):
+            assert _lib.workspace_size(B, V, dt, 512) >= _lib.FG_SAMPLE_WORKSPACE_MIN_BYTES
+    assert lib.fg_sample_workspace_size(1, 8, 9, 0) == 0         # bad dtype
+    assert lib.fg_sample_workspace_size(-1, 8, 0, 0) == 0        # bad batch
+    assert lib.fg_sample_workspace_size(1, 8, 0, -1) == 0        # bad history bound
 
 
 def test_split_mode_validation_without_gpu():
@@ -111,4 +115,3 @@ def test_split_mode_validation_without_gpu():
         assert lib.fg_sample_set_split(bad) == _lib.FG_EINVAL
     for mode in (0, 2, 1):   # ends on the default (automatic)
         assert lib.fg_sample_set_split(mode) == _lib.FG_OK
-    assert _lib.FG_SAMPLE_WORKSPACE_BYTES >= 256 * 1024

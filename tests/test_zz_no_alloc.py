@@ -1,5 +1,14 @@
 """fg_sample_noalloc: the same results as fg_sample, with no caller workspace.
 
+Some callers cannot allocate device memory at sampling time (an engine loop
+that must not allocate, a plain-FFI host without a device allocator), so the
+library offers this entry point, whose scratch is a fixed static device array.
+Its results must match fg_sample's within the parity tolerance of the other
+tests: ids equal on every row the CPU oracle does not flag as within 1e-6 of
+a CDF or top-p boundary (the two calls may take different kernels, which
+round masses at the same scale but sum them in another order), error bits
+equal on every row.
+
 Collected last (file name), and independent of the tests before it: the
 static scratch is cleared on a device's first call and every launch leaves it
 zero, so the result is the same alone and after the other tests.
@@ -13,6 +22,7 @@ import torch
 from flashgen_b200 import _lib
 from flashgen_b200.sampling.sampler import PackedParams, _DTYPES
 from flashgen_b200.workloads import make_workload
+from oracle import sampler_oracle as O
 
 
 def _args(w, logits, packed, hist, uni, out, status, workspace):
@@ -44,7 +54,10 @@ def test_noalloc_matches_fg_sample(cuda_device, cfg, batch):
     logits = w.logits.to(dev)
     hist = (torch.from_numpy(w.hist_ids).to(dev), torch.from_numpy(w.hist_offsets).to(dev))
     uni = torch.from_numpy(w.uniforms).to(dev)
-    ws = torch.zeros(_lib.FG_SAMPLE_WORKSPACE_BYTES // 4, dtype=torch.int32, device=dev)
+    need = _lib.workspace_size(w.batch, w.vocab, _DTYPES[logits.dtype], w.hist_max_len)
+    ws = torch.zeros((need + 3) // 4, dtype=torch.int32, device=dev)
+    res = O.sample_rows(w.logits, w.params, w.histories(), w.uniforms, want_kept=False)
+    flagged = res.near_u | res.near_p
     stream = torch.cuda.current_stream(dev).cuda_stream
     for call in range(2):   # two calls in a row: the scratch must come back zero
         out_a = torch.full((w.batch,), -7, dtype=torch.int64, device=dev)
@@ -56,7 +69,11 @@ def test_noalloc_matches_fg_sample(cuda_device, cfg, batch):
         assert lib.fg_sample(ctypes.byref(a), stream) == _lib.FG_OK
         assert lib.fg_sample_noalloc(ctypes.byref(b), stream) == _lib.FG_OK
         torch.cuda.synchronize(dev)
-        assert (st_b.cpu().numpy() & _lib.FG_ROW_ERROR_MASK == 0).all(), call
-        np.testing.assert_array_equal(out_b.cpu().numpy(), out_a.cpu().numpy())
-        np.testing.assert_array_equal(st_b.cpu().numpy(), st_a.cpu().numpy())
+        ids_a, ids_b = out_a.cpu().numpy(), out_b.cpu().numpy()
+        sa, sb = st_a.cpu().numpy(), st_b.cpu().numpy()
+        assert (sb & _lib.FG_ROW_ERROR_MASK == 0).all(), call
+        np.testing.assert_array_equal(sb & _lib.FG_ROW_ERROR_MASK, sa & _lib.FG_ROW_ERROR_MASK)
+        ok = (ids_a == ids_b) | flagged
+        assert ok.all(), (call, np.nonzero(~ok)[0][:8], ids_a[~ok][:8], ids_b[~ok][:8])
+        assert ((ids_b == res.ids) | flagged).all(), call
     assert (ws[:64].cpu().numpy() == 0).all()   # the row-queue counters
