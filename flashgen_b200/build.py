@@ -44,6 +44,28 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(d) <= t for d in DEPS if os.path.exists(d))
 
 
+def _includes(path: str, seen=None) -> set:
+    """The file and every local header it includes, transitively."""
+    seen = set() if seen is None else seen
+    if path in seen or not os.path.exists(path):
+        return seen
+    seen.add(path)
+    with open(path) as f:
+        for line in f:
+            line = line.strip()
+            if line.startswith("#include \""):
+                inc = line.split("\"")[1]
+                _includes(os.path.normpath(os.path.join(os.path.dirname(path), inc)), seen)
+    return seen
+
+
+def _object_current(src: str, obj: str) -> bool:
+    if not os.path.exists(obj):
+        return False
+    t = os.path.getmtime(obj)
+    return all(os.path.getmtime(d) <= t for d in _includes(src) | {os.path.abspath(__file__)})
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIBPATH
@@ -54,6 +76,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     for src in SOURCES:
         obj = os.path.join(OBJDIR, os.path.basename(src).replace(".cu", ".o"))
         objs.append(obj)
+        if not force and _object_current(src, obj):
+            continue
         cmd = [nvcc, *NVCC_FLAGS, "-c", "-o", obj, src]
         procs.append((cmd, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
     errors = []

@@ -101,8 +101,7 @@ int stream_launch(const FgSampleArgs* a, int64_t vtot, bool pen_possible, int hu
         P.off_bins = off; off += 3 * strm::NB * 4;
         P.off_ckey = off; off += 4 * P.cap;
         P.off_ccol = off; off += 4 * P.cap;
-        P.off_hcol = off; off += align_up(4 * std::max(1, P.hu_cap), 16);
-        P.off_hpen = P.off_hcol;
+        P.off_hbm = off; off += align_up(4 * (P.nwords + 1), 16);   // history column bitmap
         off = align_up(off, 128);
         P.off_ring = off;
         if (off + n * strm::TILE <= limit) { ns = n; fixed = off; break; }

@@ -1,34 +1,36 @@
 // fg_stream.cuh — the batch path of fg_sample (sm_100a): three kernels per call.
 //
 //   K1 prep_kernel     one CTA per row with penalties: the row's distinct history
-//                      columns in ascending order, with their counts, raw logits
-//                      and penalised values (FlashGen's repetition penalty, plus
-//                      presence and frequency), written to the row's workspace
-//                      block; the best penalised value (greedy rows).
+//                      columns with their counts, raw logits and penalised
+//                      values (FlashGen's repetition penalty, plus presence and
+//                      frequency), written to the row's workspace block; the
+//                      best penalised value (greedy rows) and the NaN-propagating
+//                      maximum of the penalised values.
 //   K2 stream_kernel   persistent CTAs, two per SM, each a producer warp and
 //                      NCW consumer warps. The producer takes rows from a global
 //                      queue (rows that sum exp over the whole row first) and
 //                      streams each row's 16-byte-aligned interior HBM -> shared
-//                      memory through a deep ring of 8 KB stages with 1-D bulk
-//                      async copies (cp.async.bulk, completion on mbarriers),
-//                      claiming the next row as soon as the current row's last
-//                      copy is issued. The consumers keep per tile a packed
-//                      NaN-propagating maximum, and by row class the first
+//                      memory through a ring of 16 KB stages with 1-D bulk async
+//                      copies (cp.async.bulk, completion on mbarriers), claiming
+//                      the next row as soon as the current row's last copy is
+//                      issued. A penalised row's history columns are set in a
+//                      shared-memory column bitmap and masked to -inf chunk by
+//                      chunk. Over the remaining columns the consumers keep a
+//                      packed NaN-propagating maximum, and by row class the first
 //                      argmax (greedy rows, finished here), an online sum of exp
-//                      over the raw row (top-k off), and a candidate filter
-//                      x >= tau that appends (key, column) of columns outside
-//                      the history (a binary search in the row's sorted history
-//                      list) to a shared buffer. tau starts from the tile-0
-//                      thread maxima and rises with one-pass compactions of the
-//                      buffer. At the row's end the buffer and the row's
+//                      (top-k off), and a candidate filter x >= tau that appends
+//                      (key, column) to a shared buffer. tau starts from the
+//                      tile-0 chunk maxima and rises with one-pass compactions of
+//                      the buffer. At the row's end the buffer and the row's
 //                      statistics go to the row's workspace block: the next
 //                      row's tiles are already in the ring.
 //   K3 decide_kernel   one small CTA per remaining row: the candidates plus the
 //                      penalised history entries at or above tau, the sum of exp
-//                      corrected for the history columns, then the exact K-th
-//                      largest, top-p cut and draw (integer masses, radix
-//                      selects). A row the candidates cannot decide is handed to
-//                      the cluster kernel (fg_cluster.cuh): out_ids = kDeferredId.
+//                      of the non-history columns plus the history columns'
+//                      penalised terms, then the exact K-th largest, top-p cut
+//                      and draw (integer masses, radix selects). A row the
+//                      candidates cannot decide is handed to the cluster kernel
+//                      (fg_cluster.cuh): out_ids = kDeferredId.
 //
 // Reference: flashgen/sampling/sampler.py:57-169; draw order of
 // csrc/runtime/pipeline.cpp:311-340.
@@ -65,6 +67,8 @@ struct HistHdr {
     uint32_t flags;   // FG_ROW_BAD_HISTORY / FG_ROW_BAD_PARAM
     float pbest;      // best penalised history value and its first column
     uint32_t pcol;
+    float hmax;       // NaN-propagating maximum of the penalised history values
+    uint32_t pad[3];
 };
 __host__ __device__ inline int64_t wrow_bytes(int hu_cap, int cap) {
     return (int64_t)sizeof(RowStat) + (int64_t)sizeof(HistHdr) + 12ll * ((hu_cap + 3) / 4 * 4) + 8ll * cap;
@@ -97,10 +101,10 @@ struct Params {
     int32_t hu_cap;            // history table entries (0: no penalties in this call)
     int32_t hcap4;             // hu_cap rounded up to 4
     int32_t hslots;            // K1: hash slots (power of two >= 2 * hu_cap)
-    int32_t nwords;            // K1: history bitmap words
+    int32_t nwords;            // K2: history bitmap words (columns / 32, rounded up)
     int32_t pen_possible;
     int32_t mass_shift;
-    int32_t off_ctl, off_bins, off_ckey, off_ccol, off_hcol, off_hpen, off_ring;
+    int32_t off_ctl, off_bins, off_ckey, off_ccol, off_hbm, off_ring;
 };
 
 // Parts of row r's workspace block.
@@ -161,8 +165,7 @@ struct Sm {
     uint32_t* bhi;    // [NB]
     uint32_t* ckey;
     uint32_t* ccol;
-    uint32_t* hcol;   // the row's sorted history columns (K2, K3)
-    float* hpen;      // K3: their penalised values; K1: hash / bitmap area
+    uint32_t* hbm;    // K2: bitmap of the row's history columns (nwords + 1 words)
     uint8_t* ring;
 };
 __host__ __device__ inline int bar_bytes(int ns) { return 8 * (2 * ns + 2 * RQ); }
@@ -178,8 +181,7 @@ __device__ __forceinline__ Sm carve(const Params& P) {
     s.bhi = s.blo + NB;
     s.ckey = reinterpret_cast<uint32_t*>(ssmem + P.off_ckey);
     s.ccol = reinterpret_cast<uint32_t*>(ssmem + P.off_ccol);
-    s.hcol = reinterpret_cast<uint32_t*>(ssmem + P.off_hcol);
-    s.hpen = reinterpret_cast<float*>(ssmem + P.off_hpen);
+    s.hbm = reinterpret_cast<uint32_t*>(ssmem + P.off_hbm);
     s.ring = ssmem + P.off_ring;
     return s;
 }
@@ -444,24 +446,23 @@ __device__ __forceinline__ void elem_mask_inf(uint4& v, int e) {
     }
 }
 
-// Is column c in the sorted list h[0, n)? (binary search)
-__device__ __forceinline__ bool in_sorted(const uint32_t* h, uint32_t n, uint32_t c) {
-    uint32_t lo = 0, hi = n;
-    while (lo < hi) {
-        const uint32_t mid = (lo + hi) >> 1;
-        const uint32_t v = h[mid];
-        if (v == c) return true;
-        if (v < c) lo = mid + 1; else hi = mid;
-    }
-    return false;
+// History bits of the VEC columns [c0, c0 + VEC) (bit e: column c0 + e), from
+// the row's column bitmap (one word past the last column is kept zero).
+template <int VEC>
+__device__ __forceinline__ uint32_t hist_bits(const uint32_t* bm, uint32_t c0) {
+    const uint32_t w = c0 >> 5, b = c0 & 31u;
+    uint32_t x = bm[w] >> b;
+    if (b + VEC > 32u) x |= bm[w + 1] << (32u - b);
+    return x & ((1u << VEC) - 1u);
 }
+__device__ __forceinline__ bool hist_bit(const uint32_t* bm, uint32_t c) { return (bm[c >> 5] >> (c & 31u)) & 1u; }
 
 // ===========================================================================
 // K1: history of every row with penalties
 // ===========================================================================
-// Distinct history columns with their counts (open-addressed hash), sorted
-// ascending (bitonic sort of the distinct columns only: the work follows the
-// history, not the vocabulary), their raw logits and penalised values.
+// Distinct history columns with their counts (open-addressed hash; the work
+// follows the history, not the vocabulary), their raw logits and penalised
+// values, the best penalised value and the NaN-propagating maximum.
 template <int DT>
 __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Params P) {
     using E = Elem<DT>;
@@ -473,7 +474,7 @@ __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Param
     const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms, r,
                                    has_hist, P.vocab);
     if (!p.pen) {
-        if (tid == 0) { hh->nh = 0u; hh->flags = 0u; hh->pbest = -INFINITY; hh->pcol = 0xffffffffu; }
+        if (tid == 0) { hh->nh = 0u; hh->flags = 0u; hh->pbest = -INFINITY; hh->pcol = 0xffffffffu; hh->hmax = -INFINITY; }
         return;
     }
     const Geom g = row_geom<E::SIZE>(P.logits, P.row_stride, P.vocab, r);
@@ -511,26 +512,10 @@ __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Param
     __syncthreads();
     const uint32_t total = ctl->nuniq;
     const uint32_t U = min(total, (uint32_t)P.hu_cap);
-    // bitonic sort of the U distinct columns, padded to a power of two
-    uint32_t N = 1;
-    while (N < U) N <<= 1;
-    for (uint32_t i = U + tid; i < N; i += NCT) srt[i] = 0xffffffffu;
-    __syncthreads();
-    for (uint32_t k = 2; k <= N; k <<= 1) {
-        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
-            for (uint32_t t = tid; t < N / 2; t += NCT) {
-                const uint32_t i = ((t & ~(j - 1u)) << 1) | (t & (j - 1u));
-                const uint32_t l = i + j;
-                const uint32_t a = srt[i], b = srt[l];
-                if (((i & k) == 0u) == (a > b)) { srt[i] = b; srt[l] = a; }
-            }
-            __syncthreads();
-        }
-    }
     uint32_t* hc = g_hcol(P, r);
     float* hr = g_hraw(P, r);
     float* hp = g_hpen(P, r);
-    float bv = -INFINITY;
+    float bv = -INFINITY, hm = -INFINITY;
     uint32_t bc = 0xffffffffu;
     for (uint32_t i = tid; i < U; i += NCT) {
         const uint32_t c = srt[i];
@@ -542,8 +527,10 @@ __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Param
         const float raw = E::load(g.row, c);
         const float pen = penalize(p, raw, count);
         hc[i] = c; hr[i] = raw; hp[i] = pen;
+        hm = fmax_nan(hm, pen);
         if (arg_better(pen, c, bv, bc)) { bv = pen; bc = c; }
     }
+    hm = c_max_nan(hm, s);
     // the best penalised value (first column on ties)
     const int lane = tid & 31, wid = tid >> 5;
 #pragma unroll
@@ -565,6 +552,7 @@ __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Param
         hh->flags = fl;
         hh->pbest = v;
         hh->pcol = c;
+        hh->hmax = hm;
     }
 }
 
@@ -598,13 +586,13 @@ __device__ __forceinline__ void zadd(St& st, float x) {
 }
 
 // One tile's chunks. CLS: RC_GREEDY, RC_TOPK or RC_NUCLEUS (also for
-// RC_FULL). PEN: the row has history columns: the argmax skips them (a
-// search in the row's sorted list, only when a new maximum appears); the
-// candidates and the sum of exp take the raw row, and K3 swaps the history
-// columns' raw values for their penalised ones.
+// RC_FULL). PEN: the row has history columns; a chunk's history elements are
+// set to -inf (one bitmap word per chunk), so the maximum, the argmax, the
+// candidates and the sum of exp cover the non-history columns only, and K3
+// adds the history columns with their penalised values.
 template <int DT, int CLS, bool PEN>
 __device__ __forceinline__ void tile_chunks(const Params& P, const Sm& s, const uint4 (&v)[CPT], int nch, int tcol0,
-                                            uint32_t U, St& st) {
+                                            St& st) {
     constexpr int VEC = Elem<DT>::VEC;
     const int tid = threadIdx.x;
 #pragma unroll
@@ -612,16 +600,23 @@ __device__ __forceinline__ void tile_chunks(const Params& P, const Sm& s, const 
         const int ch = tid + j * NCT;
         if (ch >= nch) continue;
         const int c0 = tcol0 + ch * VEC;
-        const float cm = chunk_max<DT>(v[j]);
+        uint4 x = v[j];
+        if (PEN) {
+            const uint32_t hb = hist_bits<VEC>(s.hbm, (uint32_t)c0);
+            if (hb) {
+#pragma unroll
+                for (int e = 0; e < VEC; ++e)
+                    if ((hb >> e) & 1u) elem_mask_inf<DT>(x, e);
+            }
+        }
+        const float cm = chunk_max<DT>(x);
         st.mx = fmax_nan(st.mx, cm);
         if constexpr (CLS == RC_GREEDY) {
             if (cm > st.bv) {
 #pragma unroll
                 for (int e = 0; e < VEC; ++e) {
-                    const float x = elem_at<DT>(v[j], e);
-                    if (x > st.bv && !(PEN && in_sorted(s.hcol, U, (uint32_t)(c0 + e)))) {
-                        st.bv = x; st.bc = (uint32_t)(c0 + e);
-                    }
+                    const float xe = elem_at<DT>(x, e);
+                    if (xe > st.bv) { st.bv = xe; st.bc = (uint32_t)(c0 + e); }
                 }
             }
         } else {
@@ -634,22 +629,21 @@ __device__ __forceinline__ void tile_chunks(const Params& P, const Sm& s, const 
                 }
 #pragma unroll
                 for (int e = 0; e < VEC; e += 2) {
-                    st.z0 += ex2f_approx(__fmaf_rn(elem_at<DT>(v[j], e), st.c, st.nzc));
-                    st.z1 += ex2f_approx(__fmaf_rn(elem_at<DT>(v[j], e + 1), st.c, st.nzc));
+                    st.z0 += ex2f_approx(__fmaf_rn(elem_at<DT>(x, e), st.c, st.nzc));
+                    st.z1 += ex2f_approx(__fmaf_rn(elem_at<DT>(x, e + 1), st.c, st.nzc));
                 }
             }
             if (cm >= st.tau) {
-                // every element at or above tau, history columns included (K3
-                // replaces them by their penalised values): one atomic per chunk
+                // every element at or above tau: one atomic per chunk
                 uint32_t msk = 0u;
 #pragma unroll
-                for (int e = 0; e < VEC; ++e) msk |= (elem_at<DT>(v[j], e) >= st.tau ? 1u : 0u) << e;
+                for (int e = 0; e < VEC; ++e) msk |= (elem_at<DT>(x, e) >= st.tau ? 1u : 0u) << e;
                 uint32_t pos = atomicAdd(&s.ctl->ncand, (uint32_t)__popc(msk));
 #pragma unroll
                 for (int e = 0; e < VEC; ++e) {
                     if (!((msk >> e) & 1u)) continue;
                     if (pos < (uint32_t)P.cap) {
-                        s.ckey[pos] = fkey(elem_at<DT>(v[j], e));
+                        s.ckey[pos] = fkey(elem_at<DT>(x, e));
                         s.ccol[pos] = (uint32_t)(c0 + e);
                     } else {
                         s.ctl->ovf = 1u;
@@ -825,7 +819,7 @@ __device__ void producer(const Params& P) {
 struct Ring { uint32_t st, ph; };
 
 template <int DT, int CLS, bool PEN>
-__device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st_io, int kt, uint32_t U) {
+__device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st_io, int kt) {
     using E = Elem<DT>;
     constexpr int ESZ = E::SIZE;
     const Sm s = carve(P);
@@ -836,10 +830,11 @@ __device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st
     const int nt = (int)((g.ibytes + TILE - 1) / TILE);
     St st = st_io;
     volatile int* abort = &s.ctl->abort;
-    // the buffer may hold up to U history columns with raw values: keep kt
-    // non-history entries above tau by keeping kt + U
-    const int kt2 = min(kt + (int)U, P.cap / 2);
-    uint32_t trig = (uint32_t)min(P.cap * 3 / 4, max(2 * kt2 + 256, 1024));
+    // the buffer holds non-history columns only: compactions keep kt entries.
+    // The count is checked after every tile; a compaction starts while a
+    // quarter of the buffer is still free, so a tile rarely overflows it.
+    const int kt2 = min(kt, P.cap / 2);
+    uint32_t trig = (uint32_t)min(P.cap * 3 / 4, max(2 * kt2 + 256, 512));
     for (int t = 0; t < nt; ++t) {
         const bool ok = mbar_wait(&s.full[rg.st], rg.ph, abort);
         if (!ok) *abort = 1;
@@ -857,10 +852,9 @@ __device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st
         if (++rg.st == ns) { rg.st = 0; rg.ph ^= 1u; }
         const int tcol0 = g.head + t * (TILE / ESZ);
         if (CLS != RC_GREEDY && t == 0) st.tau = tile0_tau<DT>(P, kt, nch, v[0], v[1], v[2], v[3]);
-        tile_chunks<DT, CLS, PEN>(P, s, v, nch, tcol0, U, st);
+        tile_chunks<DT, CLS, PEN>(P, s, v, nch, tcol0, st);
         if (CLS != RC_GREEDY) {
-            const bool check = t < 4 || (t < 16 && (t & 1)) || (t & 3) == 3 || t == nt - 1;
-            if (check) {
+            {
                 csync();
                 const uint32_t n = s.ctl->ncand;
                 const bool ovf = s.ctl->ovf != 0u;
@@ -868,12 +862,13 @@ __device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st
                 if (ovf) {
                     st.cand = false;
                 } else if (st.cand && n > trig) {
+                    if (tid == 0) s.ctl->tau = st.tau;   // the compaction only raises it
                     const uint32_t m = compact(P, r, n, kt2);
                     if (tid == 0) s.ctl->ncand = m;
                     st.tau = s.ctl->tau;
                     csync();
                     // ties may keep the count up: compact again only after 512 more
-                    if (m + 512u > trig) trig = min((uint32_t)P.cap - 256u, m + 512u);
+                    if (m + 512u > trig) trig = min((uint32_t)P.cap * 3 / 4, m + 512u);
                 }
             }
         }
@@ -882,7 +877,7 @@ __device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st
 }
 
 template <int DT, int CLS, bool PEN>
-__device__ __noinline__ void sample_row_cls(const Params& P, int r, Ring& rg, uint32_t U) {
+__device__ __noinline__ void sample_row_cls(const Params& P, int r, Ring& rg) {
     using E = Elem<DT>;
     constexpr int ESZ = E::SIZE;
     const Sm s = carve(P);
@@ -896,20 +891,22 @@ __device__ __noinline__ void sample_row_cls(const Params& P, int r, Ring& rg, ui
     st.c = p.temp_on ? __fdiv_rn(kL2E, p.T) : kL2E;
     st.zm = -1e30f; st.nzc = -(st.zm * st.c); st.z0 = 0.0f; st.z1 = 0.0f;
     st.tau = -INFINITY; st.cand = true;
-    stream_row<DT, CLS, PEN>(P, r, rg, st, kt, U);
+    stream_row<DT, CLS, PEN>(P, r, rg, st, kt);
     // the ragged head / tail (fewer than VEC each)
     {
         const int nh = g.head, ntl = P.vocab - g.tail0;
         if (tid < nh + ntl) {
             const int c = tid < nh ? tid : g.tail0 + (tid - nh);
             const float x = E::load(g.row, c);
-            const bool hist = CLS == RC_GREEDY && PEN && in_sorted(s.hcol, U, (uint32_t)c);
-            st.mx = fmax_nan(st.mx, x);
-            if (CLS == RC_GREEDY) {
-                if (!hist && arg_better(x, (uint32_t)c, st.bv, st.bc)) { st.bv = x; st.bc = (uint32_t)c; }
-            } else {
-                if (CLS == RC_NUCLEUS) zadd(st, x);
-                if (st.cand && x >= st.tau) append(P, s, x, (uint32_t)c);
+            const bool hist = PEN && hist_bit(s.hbm, (uint32_t)c);
+            if (!hist) {
+                st.mx = fmax_nan(st.mx, x);
+                if (CLS == RC_GREEDY) {
+                    if (arg_better(x, (uint32_t)c, st.bv, st.bc)) { st.bv = x; st.bc = (uint32_t)c; }
+                } else {
+                    if (CLS == RC_NUCLEUS) zadd(st, x);
+                    if (st.cand && x >= st.tau) append(P, s, x, (uint32_t)c);
+                }
             }
         }
     }
@@ -926,16 +923,18 @@ __device__ __noinline__ void sample_row_cls(const Params& P, int r, Ring& rg, ui
         if (tid == 0) {
             int status = p.bad | FG_ROW_GREEDY;
             int64_t out = -1;
+            float Mf = M;   // the maximum after penalties
             if (PEN) {
                 const HistHdr* hh = hist_hdr(P, r);
                 status |= (int)hh->flags;
+                Mf = fmax_nan(M, hh->hmax);
                 if (arg_better(hh->pbest, hh->pcol, bv, bc)) { bv = hh->pbest; bc = hh->pcol; }
             }
             bool defer = false;
             if (aborted) status |= FG_ROW_TIMEOUT;
             else if (status & (FG_ROW_BAD_PARAM | FG_ROW_BAD_UNIFORM)) out = -1;
-            else if (M != M) defer = true;            // the first NaN: the cluster kernel finds it
-            else out = (M == -INFINITY) ? 0 : (int64_t)bc;
+            else if (Mf != Mf) defer = true;          // the first NaN: the cluster kernel finds it
+            else out = (Mf == -INFINITY) ? 0 : (int64_t)bc;
             if (defer) {
                 P.out_ids[r] = kDeferredId;
             } else {
@@ -977,6 +976,8 @@ __device__ void consumer(const Params& P) {
     const Sm s = carve(P);
     const int tid = threadIdx.x;
     Ring rg{0u, 0u};
+    if (P.pen_possible)
+        for (int i = tid; i <= P.nwords; i += NCT) s.hbm[i] = 0u;   // ordered by the loop's first barrier
     volatile int* abort = &s.ctl->abort;
     for (uint32_t k = 0;; ++k) {
         const uint32_t slot = k % RQ, ph = (k / RQ) & 1u;
@@ -1008,23 +1009,28 @@ __device__ void consumer(const Params& P) {
         }
         if (tid == 0) { s.ctl->ncand = 0u; s.ctl->ovf = 0u; s.ctl->tau = -INFINITY; }
         uint32_t U = 0;
+        const uint32_t* hc = nullptr;
         if (p.pen) {
-            // the row's history size from K1, and for greedy rows its sorted columns
+            // the row's history columns from K1 into the (all-zero) bitmap: the
+            // stream leaves them out, K3 adds their penalised values
             U = min(hist_hdr(P, r)->nh, (uint32_t)P.hu_cap);
-            if (p.cls == RC_GREEDY) {
-                const uint32_t* hc = g_hcol(P, r);
-                for (uint32_t i = tid; i < U; i += NCT) s.hcol[i] = hc[i];
+            hc = g_hcol(P, r);
+            for (uint32_t i = tid; i < U; i += NCT) {
+                const uint32_t c = __ldcg(hc + i);
+                atomicOr(&s.hbm[c >> 5], 1u << (c & 31u));
             }
         }
         csync();
         if (p.pen) {
-            if (p.cls == RC_GREEDY) sample_row_cls<DT, RC_GREEDY, true>(P, r, rg, U);
-            else if (p.cls == RC_TOPK) sample_row_cls<DT, RC_TOPK, true>(P, r, rg, U);
-            else sample_row_cls<DT, RC_NUCLEUS, true>(P, r, rg, U);
+            if (p.cls == RC_GREEDY) sample_row_cls<DT, RC_GREEDY, true>(P, r, rg);
+            else if (p.cls == RC_TOPK) sample_row_cls<DT, RC_TOPK, true>(P, r, rg);
+            else sample_row_cls<DT, RC_NUCLEUS, true>(P, r, rg);
+            // sample_row_cls ends with a barrier: every lookup of this row is done
+            for (uint32_t i = tid; i < U; i += NCT) s.hbm[__ldcg(hc + i) >> 5] = 0u;
         } else {
-            if (p.cls == RC_GREEDY) sample_row_cls<DT, RC_GREEDY, false>(P, r, rg, 0u);
-            else if (p.cls == RC_TOPK) sample_row_cls<DT, RC_TOPK, false>(P, r, rg, 0u);
-            else sample_row_cls<DT, RC_NUCLEUS, false>(P, r, rg, 0u);
+            if (p.cls == RC_GREEDY) sample_row_cls<DT, RC_GREEDY, false>(P, r, rg);
+            else if (p.cls == RC_TOPK) sample_row_cls<DT, RC_TOPK, false>(P, r, rg);
+            else sample_row_cls<DT, RC_NUCLEUS, false>(P, r, rg);
         }
         if (*abort) break;
     }
@@ -1252,21 +1258,24 @@ __global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Par
         (void)scale;
         int status = p.bad;
         uint32_t U = 0;
+        // Mraw: the maximum of the non-history columns (K2); Mf: after penalties
+        const float Mraw = rs.mraw;
+        float Mf = Mraw;
         if (p.pen) {
             const HistHdr* hh = hist_hdr(P, r);
             status |= (int)hh->flags;
             U = min(hh->nh, (uint32_t)P.hu_cap);
+            Mf = fmax_nan(Mraw, hh->hmax);
         }
         bool defer = rs.ovf != 0u;
         int64_t out = -1;
-        const float Mraw = rs.mraw;
         if (status & (FG_ROW_BAD_PARAM | FG_ROW_BAD_UNIFORM)) {
             defer = false;
-        } else if (Mraw != Mraw) {
+        } else if (Mf != Mf) {
             status |= FG_ROW_NAN; defer = false;
-        } else if (Mraw == INFINITY) {
+        } else if (Mf == INFINITY) {
             status |= FG_ROW_POS_INF; defer = false;
-        } else if (Mraw == -INFINITY) {
+        } else if (Mf == -INFINITY) {
             status |= FG_ROW_ALL_MASKED; defer = false;
         } else if (!defer) {
             // the decision set: the candidates (non-history, raw = final) and the
@@ -1275,48 +1284,19 @@ __global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Par
             uint32_t n = min(rs.n, (uint32_t)P.cap);
             const uint32_t* gk = g_ckey(P, r);
             const uint32_t* gc = g_ccol(P, r);
-            if (p.pen) {
-                // the row's sorted history columns, then the candidates without them
-                const uint32_t* hcg = g_hcol(P, r);
-                for (uint32_t i = tid; i < U; i += NCT) s.hcol[i] = hcg[i];
-                if (tid == 0) s.ctl->ncand = 0u;
-                csync();
-                for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
-                    const uint32_t i = i0 + tid;
-                    const bool keep = i < n && !in_sorted(s.hcol, U, gc[i]);
-                    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-                    uint32_t base = 0;
-                    if ((tid & 31) == 0 && bal) base = atomicAdd(&s.ctl->ncand, (uint32_t)__popc(bal));
-                    base = __shfl_sync(0xffffffffu, base, 0);
-                    if (keep) {
-                        const uint32_t pos = base + (uint32_t)__popc(bal & ((1u << (tid & 31)) - 1u));
-                        s.ckey[pos] = gk[i];
-                        s.ccol[pos] = gc[i];
-                    }
-                }
-                csync();
-                n = s.ctl->ncand;
-                csync();
-            } else {
-                for (uint32_t i = tid; i < n; i += NCT) { s.ckey[i] = gk[i]; s.ccol[i] = gc[i]; }
-            }
+            // the candidates hold no history column (K2 leaves them out)
+            for (uint32_t i = tid; i < n; i += NCT) { s.ckey[i] = gk[i]; s.ccol[i] = gc[i]; }
             if (tid == 0) { s.ctl->ncand = n; s.ctl->tau = tau; s.ctl->ovf = 0u; }
             csync();
-            double hcorr = 0.0, hraw = 0.0;
+            // history entries at or above tau join the set
             float hmax = -INFINITY;
             if (p.pen) {
                 const uint32_t* hc = g_hcol(P, r);
-                const float* hr = g_hraw(P, r);
                 const float* hp = g_hpen(P, r);
-                const double c = (double)(p.temp_on ? __fdiv_rn(kL2E, p.T) : kL2E);
                 for (uint32_t i = tid; i < U; i += NCT) {
                     const float pen = hp[i];
                     hmax = fmax_nan(hmax, pen);
                     if (pen >= tau) append(P, s, pen, hc[i]);
-                    if (p.cls != RC_TOPK) {
-                        hraw += exp2(((double)hr[i] - (double)Mraw) * c);
-                        hcorr += exp2(((double)pen - (double)Mraw) * c);
-                    }
                 }
             }
             hmax = c_max_nan(hmax, s);
@@ -1326,8 +1306,8 @@ __global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Par
             csync();
             if (!defer) {
                 // the row's maximum after penalties: every value at or above tau is
-                // in the set, and the raw maximum of the non-history columns is
-                // one of them unless the set is empty
+                // in the set, and the maximum of the non-history columns is one of
+                // them unless the set is empty
                 float cmax = -INFINITY;
                 for (uint32_t i = tid; i < n; i += NCT) cmax = fmaxf(cmax, funkey(s.ckey[i]));
                 cmax = c_max_nan(cmax, s);
@@ -1337,17 +1317,17 @@ __global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Par
                 } else {
                     double Zd = 0.0;
                     if (p.cls != RC_TOPK) {
-                        const double hr_t = c_sum_f64(hraw, s);
-                        const double hc_t = c_sum_f64(hcorr, s);
-                        // the raw row's sum without the history columns' raw terms,
-                        // with their penalised terms; relative to M
-                        const double zr = rs.zr;
-                        if (hr_t > 0.5 * zr) {
-                            defer = true;   // most of the raw mass sat on history columns
-                        } else {
-                            const double c = (double)(p.temp_on ? __fdiv_rn(kL2E, p.T) : kL2E);
-                            Zd = (zr - hr_t + hc_t) * exp2(((double)Mraw - (double)M) * c);
+                        // the non-history sum of exp (relative to Mraw) plus the
+                        // history columns' penalised terms, relative to M
+                        const double c = (double)(p.temp_on ? __fdiv_rn(kL2E, p.T) : kL2E);
+                        double hz = 0.0;
+                        if (p.pen) {
+                            const float* hp = g_hpen(P, r);
+                            for (uint32_t i = tid; i < U; i += NCT) hz += exp2(((double)hp[i] - (double)M) * c);
                         }
+                        const double hz_t = c_sum_f64(hz, s);
+                        const double zr = rs.zr;
+                        Zd = hz_t + (zr > 0.0 ? zr * exp2(((double)Mraw - (double)M) * c) : 0.0);
                     }
                     if (!defer) {
                         const Fin fo = finish_sampling(P, r, n, M, Zd, M);
