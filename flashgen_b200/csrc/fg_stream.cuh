@@ -656,11 +656,11 @@ __device__ __forceinline__ void tile_chunks(const Params& P, const Sm& s, const 
 }
 
 // Starting threshold: a lower bound of the K0-th largest element of the first
-// tile (K0 its share of the row's target, with a margin): a 256-bin histogram
-// of the tile's chunk maxima over their key range gives the lowest key of the
-// bin that holds the K0-th largest maximum; at least K0 chunks, hence K0
-// elements, lie at or above it. -inf when the tile has fewer chunks. A guess
-// for the row: the decision checks that the candidates hold the K-th largest.
+// tile (K0 its share of the row's target, with a margin): histograms of the
+// tile's chunk maxima give the lowest key of the bin that holds the K0-th
+// largest maximum; at least K0 chunks, hence K0 elements, lie at or above it.
+// -inf when the tile has fewer chunks. A guess for the row: the decision
+// checks that the candidates hold the K-th largest.
 template <int DT>
 __device__ __noinline__ float tile0_tau(const Params& P, int kt, int nch, uint4 v0, uint4 v1, uint4 v2, uint4 v3) {
     static_assert(CPT == 4, "tile0_tau takes CPT chunks by value");
@@ -683,20 +683,32 @@ __device__ __noinline__ float tile0_tau(const Params& P, int kt, int nch, uint4 
     const int K0 = (int)min((int64_t)nch, min((int64_t)kt, share));
     c_minmax_u32(kmin, kmax, s);
     if (kmin > kmax || K0 < 1) return -INFINITY;
-    const int vb = varying_bits(0u, kmax - kmin);
-    const int shift = vb > 8 ? vb - 8 : 0;
-    for (int b = tid; b < NB; b += NCT) s.bcnt[b] = 0u;
-    csync();
+    // two rounds of a 256-bin histogram: the whole key range, then the bin that
+    // holds the K0-th largest maximum (a range that crosses zero or spans many
+    // binades leaves the first round's bins too coarse)
+    uint32_t lo = kmin, hi = kmax;
+    uint64_t rank = (uint64_t)(K0 - 1);
+    for (int round = 0; round < 2; ++round) {
+        const int vb = varying_bits(0u, hi - lo);
+        const int shift = vb > 8 ? vb - 8 : 0;
+        for (int b = tid; b < NB; b += NCT) s.bcnt[b] = 0u;
+        csync();
 #pragma unroll
-    for (int j = 0; j < CPT; ++j)
-        if (km[j] != 0u) atomicAdd(&s.bcnt[(km[j] - kmin) >> shift], 1u);
-    csync();
-    if (tid < 32) scan_desc<false>(s, NB, (uint64_t)(K0 - 1));
-    csync();
-    const SelRes rr = s.ctl->sel;
-    csync();
-    if (!rr.ok) return -INFINITY;
-    return funkey(kmin + (rr.key << shift));
+        for (int j = 0; j < CPT; ++j)
+            if (km[j] != 0u && km[j] >= lo && km[j] <= hi) atomicAdd(&s.bcnt[(km[j] - lo) >> shift], 1u);
+        csync();
+        if (tid < 32) scan_desc<false>(s, NB, rank);
+        csync();
+        const SelRes rr = s.ctl->sel;
+        csync();
+        if (!rr.ok) return -INFINITY;
+        const uint32_t blo = lo + (rr.key << shift);
+        if (shift == 0) return funkey(blo);
+        rank -= rr.before;
+        hi = min(hi, blo + ((1u << shift) - 1u));
+        lo = blo;
+    }
+    return funkey(lo);
 }
 
 // Compaction in one pass: a 256-bin histogram of the buffer's keys over their
