@@ -19,7 +19,7 @@ struct DevInfo {
     int smem_optin = 0;
     int smem_per_sm = 0;
     // one-time kernel attributes, per kernel family (see the K_* ids) and dtype
-    bool attr_set[5][3] = {};
+    bool attr_set[6][3] = {};
     // cluster kernel: co-resident clusters per (dtype, cluster size) for the
     // shared-memory size it was last queried with
     int cl_smem[3][17] = {};
@@ -27,7 +27,7 @@ struct DevInfo {
     bool ok = false;
 };
 constexpr int kMaxDevices = 64;
-enum KernelFamily { K_ROW = 0, K_STREAM = 1, K_CLUSTER = 2, K_PREP = 3, K_DECIDE = 4 };
+enum KernelFamily { K_ROW = 0, K_STREAM = 1, K_CLUSTER = 2, K_PREP = 3, K_DECIDE = 4, K_DEEP = 5 };
 
 // Attributes of the current device (queried once per device, cached).
 int device_info(DevInfo** out);

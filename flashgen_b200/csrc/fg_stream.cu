@@ -1,6 +1,7 @@
 // fg_stream.cu — host launch of the batch path (fg_stream.cuh): K1 (history
-// lists, when the call has penalties), K2 (the stream), K3 (decisions), then
-// the cluster kernel over the rows K3 defers. All on the caller's stream.
+// lists, when the call has penalties), K2 (the stream), K3 (decisions), K4
+// (16-bit rows whose cut or draw lies below the candidates), then the cluster
+// kernel over the rows K3 and K4 defer. All on the caller's stream.
 #include <algorithm>
 
 #include "fg_internal.h"
@@ -18,7 +19,11 @@ template <class K>
 int set_smem_attr(K kern, DevInfo* d, int family, int dt) {
     if (d->attr_set[family][dt]) return FG_OK;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->smem_optin) != cudaSuccess)
+    // the dynamic share of the opt-in limit: what the kernel's static shared memory leaves
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return FG_EDEVICE;
+    const int dyn = d->smem_optin - (int)fa.sharedSizeBytes;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess)
         return FG_EDEVICE;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                              (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
@@ -37,7 +42,8 @@ int hslots_of(int hu_cap) {
 }
 
 template <int DT>
-int launch_all(strm::Params& P, int k2_smem, int k2_grid, int k1_smem, int k3_smem, cudaStream_t st, DevInfo* d) {
+int launch_all(strm::Params& P, int k2_smem, int k2_grid, int k1_smem, int k3_smem, int k4_smem, cudaStream_t st,
+               DevInfo* d) {
     int rc;
     if (P.pen_possible) {
         rc = set_smem_attr(strm::prep_kernel<DT>, d, K_PREP, DT);
@@ -53,7 +59,17 @@ int launch_all(strm::Params& P, int k2_smem, int k2_grid, int k1_smem, int k3_sm
     if (rc != FG_OK) return rc;
     const int k3_grid = std::max(1, std::min(P.batch, d->sms * 8));
     strm::decide_kernel<DT><<<k3_grid, strm::NCT, k3_smem, st>>>(P);
-    return cudaGetLastError() == cudaSuccess ? FG_OK : FG_ELAUNCH;
+    if (cudaGetLastError() != cudaSuccess) return FG_ELAUNCH;
+    if constexpr (DT != FG_DTYPE_F32) {
+        // K4: 16-bit rows whose top-p cut or draw lies below the candidates
+        rc = set_smem_attr(strm::deep_kernel<DT>, d, K_DEEP, DT);
+        if (rc != FG_OK) return rc;
+        strm::deep_kernel<DT><<<k3_grid, strm::NCT, k4_smem, st>>>(P);
+        if (cudaGetLastError() != cudaSuccess) return FG_ELAUNCH;
+    } else {
+        (void)k4_smem;
+    }
+    return FG_OK;
 }
 
 }  // namespace
@@ -84,7 +100,7 @@ int stream_launch(const FgSampleArgs* a, int64_t vtot, bool pen_possible, int hu
     P.mass_shift = 62 - bits_for(a->vocab);
     P.cap = kCap;
     P.k_fast = kCap / 2;
-    P.k_nuc = kCap / 2;
+    P.k_nuc = kCap * 3 / 8;
     // the workspace holds a block per row after the counters
     P.wrow_bytes = strm::wrow_bytes(P.hu_cap, P.cap);
     const size_t need = 256 + (size_t)a->batch * (size_t)P.wrow_bytes;
@@ -109,15 +125,20 @@ int stream_launch(const FgSampleArgs* a, int64_t vtot, bool pen_possible, int hu
     if (ns == 0) return FG_ENOTSUP;
     P.nstage = ns;
     const int k2_smem = fixed + ns * strm::TILE;
-    const int k3_smem = fixed;                       // everything but the ring
+    const int k3_smem = P.off_hbm;                   // control, bins and the candidate buffer
+    P.off_cnt = align_up(P.off_hbm + 4 * (P.nwords + 1), 16);
+    P.off_tsum = P.off_cnt + 4 * strm::NBIN;
+    P.off_hl = P.off_tsum + 8 * (strm::NCT + strm::SLOTS);
+    const int k4_smem = P.off_hl + 8 * strm::HL_MAX;
+    if (k4_smem + strm::kDeepStaticSmem > d->smem_optin) return FG_ENOTSUP;
     const int k1_smem = align_up(P.off_ctl + (int)sizeof(strm::Ctl), 16) + 8 * P.hslots + 4 * (P.hslots / 2);
     if (pen_possible && k1_smem > d->smem_optin) return FG_ENOTSUP;
     const int k2_grid = std::max(1, std::min(a->batch, d->sms * per_sm));
     int rc;
     switch (a->dtype) {
-        case FG_DTYPE_F32: rc = launch_all<FG_DTYPE_F32>(P, k2_smem, k2_grid, k1_smem, k3_smem, st, d); break;
-        case FG_DTYPE_F16: rc = launch_all<FG_DTYPE_F16>(P, k2_smem, k2_grid, k1_smem, k3_smem, st, d); break;
-        default: rc = launch_all<FG_DTYPE_BF16>(P, k2_smem, k2_grid, k1_smem, k3_smem, st, d); break;
+        case FG_DTYPE_F32: rc = launch_all<FG_DTYPE_F32>(P, k2_smem, k2_grid, k1_smem, k3_smem, k4_smem, st, d); break;
+        case FG_DTYPE_F16: rc = launch_all<FG_DTYPE_F16>(P, k2_smem, k2_grid, k1_smem, k3_smem, k4_smem, st, d); break;
+        default: rc = launch_all<FG_DTYPE_BF16>(P, k2_smem, k2_grid, k1_smem, k3_smem, k4_smem, st, d); break;
     }
     if (rc != FG_OK) return rc;
     const int gm = cluster_size_for(a, d, 2);

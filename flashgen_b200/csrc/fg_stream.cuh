@@ -51,6 +51,7 @@ constexpr int NB = 256;                 // radix bins
 constexpr int BAR = 1;                  // named barrier of the consumer warps
 constexpr uint32_t kSkip = 0x80000000u; // row-queue flag: the row is not streamed
 constexpr int64_t kPendingId = -3;      // out_ids of a row K2 leaves to K3
+constexpr int64_t kDeepId = -4;         // out_ids of a row K3 leaves to K4
 
 // Per-row workspace block (16-byte aligned parts):
 //   RowStat, HistHdr, hcol[hu_cap], hraw[hu_cap], hpen[hu_cap], ckey[cap], ccol[cap]
@@ -61,6 +62,11 @@ struct RowStat {
     uint32_t n;       // candidates
     uint32_t ovf;     // the buffer overflowed: incomplete
     uint32_t pad[2];
+    // K3 -> K4 (rows whose cut or draw lies below the candidates)
+    double zq;        // the row's total mass (mass units, from the sums of exp)
+    unsigned long long ac;   // exact mass of the candidate set
+    float mfin;       // the row's maximum after penalties
+    uint32_t pad2[3];
 };
 struct HistHdr {
     uint32_t nh;      // distinct history columns kept (<= hu_cap)
@@ -105,6 +111,7 @@ struct Params {
     int32_t pen_possible;
     int32_t mass_shift;
     int32_t off_ctl, off_bins, off_ckey, off_ccol, off_hbm, off_ring;
+    int32_t off_cnt, off_tsum, off_hl;   // K4: key counts, per-thread masses, history entries
 };
 
 // Parts of row r's workspace block.
@@ -679,7 +686,7 @@ __device__ __noinline__ float tile0_tau(const Params& P, int kt, int nch, uint4 
         km[j] = fkey(cm);
         kmin = min(kmin, km[j]); kmax = max(kmax, km[j]);
     }
-    const int64_t share = ((int64_t)2 * kt * (int64_t)(nch * VEC) + P.vocab - 1) / P.vocab + 16;
+    const int64_t share = ((int64_t)3 * kt * (int64_t)(nch * VEC) + 2 * P.vocab - 1) / (2 * P.vocab) + 8;
     const int K0 = (int)min((int64_t)nch, min((int64_t)kt, share));
     c_minmax_u32(kmin, kmax, s);
     if (kmin > kmax || K0 < 1) return -INFINITY;
@@ -1107,6 +1114,9 @@ struct Fin {
     int64_t id;
     int status;
     bool defer;
+    bool deep;          // deferred because the cut or the draw lies below the candidates
+    double zq;          // then: the row's total mass and the candidates' mass
+    uint64_t ac;
 };
 __device__ __noinline__ Fin finish_sampling(const Params& P, int r, uint32_t n, float M, double Zd, float zmax) {
     const Sm s = carve(P);
@@ -1115,7 +1125,7 @@ __device__ __noinline__ Fin finish_sampling(const Params& P, int r, uint32_t n, 
     const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms, r,
                                    has_hist, P.vocab);
     Fin fo;
-    fo.id = -1; fo.status = 0; fo.defer = false;
+    fo.id = -1; fo.status = 0; fo.defer = false; fo.deep = false; fo.zq = 0.0; fo.ac = 0;
     const float scale = __uint_as_float((uint32_t)(127 + P.mass_shift) << 23);
     const float My = ydiv(p, M);
     const uint32_t ktau = fkey(s.ctl->tau);
@@ -1188,7 +1198,10 @@ __device__ __noinline__ Fin finish_sampling(const Params& P, int r, uint32_t n, 
         const double Zq = Zd * exp((double)zmax / (double)p.T - (double)My) * (double)scale;
         if (p.use_p) {
             const uint64_t Pt = (uint64_t)floor((double)p.top_p * Zq);
-            if (Pt >= AC) { fo.defer = true; return fo; }   // the cut lies below the buffer
+            if (Pt >= AC) {   // the cut lies below the buffer
+                fo.defer = true; fo.deep = true; fo.zq = Zq; fo.ac = AC;
+                return fo;
+            }
             const Sel so = c_select<true>(s, [&](auto&& f) {
                 for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
                     const uint32_t i = i0 + tid;
@@ -1206,7 +1219,10 @@ __device__ __noinline__ Fin finish_sampling(const Params& P, int r, uint32_t n, 
         } else {
             Qf = (uint64_t)Zq;
             const uint64_t Dt0 = (uint64_t)floor((double)p.u * (double)Qf);
-            if (Dt0 >= AC) { fo.defer = true; return fo; }   // the draw lies below the buffer
+            if (Dt0 >= AC) {   // the draw lies below the buffer
+                fo.defer = true; fo.deep = true; fo.zq = Zq; fo.ac = AC;
+                return fo;
+            }
         }
     }
     if (Qf == 0) { fo.defer = true; return fo; }
@@ -1279,7 +1295,7 @@ __global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Par
             U = min(hh->nh, (uint32_t)P.hu_cap);
             Mf = fmax_nan(Mraw, hh->hmax);
         }
-        bool defer = rs.ovf != 0u;
+        bool defer = rs.ovf != 0u, deep = false;
         int64_t out = -1;
         if (status & (FG_ROW_BAD_PARAM | FG_ROW_BAD_UNIFORM)) {
             defer = false;
@@ -1344,6 +1360,14 @@ __global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Par
                     if (!defer) {
                         const Fin fo = finish_sampling(P, r, n, M, Zd, M);
                         if (fo.defer) defer = true;
+                        if (fo.deep && DT != FG_DTYPE_F32) {
+                            // K4 continues below the candidates (16-bit logits)
+                            deep = true;
+                            if (tid == 0) {
+                                RowStat* w = row_stat(P, r);
+                                w->zq = fo.zq; w->ac = fo.ac; w->mfin = M;
+                            }
+                        }
                         else out = fo.id;
                     }
                 }
@@ -1351,10 +1375,476 @@ __global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Par
         }
         if (tid == 0) {
             if (defer) {
-                P.out_ids[r] = kDeferredId;
+                P.out_ids[r] = deep ? kDeepId : kDeferredId;
             } else {
                 P.out_ids[r] = out >= 0 ? out + P.vocab_offset : -1;
                 if (out < 0 && !(status & FG_ROW_ERROR_MASK)) status |= FG_ROW_ALL_MASKED;
+                if (P.out_status) P.out_status[r] = status;
+            }
+        }
+        csync();
+    }
+}
+
+
+// ===========================================================================
+// K4: 16-bit rows whose top-p cut or draw lies below the candidates
+// (out_ids == kDeepId). Below tau every non-history value is one of the
+// 65536 16-bit values, and equal values have equal masses, so one counting
+// pass over the row gives exact masses: count(key) * mass(value) for the
+// NBIN keys right below tau. The history columns below tau join with their
+// penalised values. A descending scan finds the element at which the
+// cumulative mass reaches a target; a second pass finds the j-th column
+// (ascending) of a value's elements. Rows outside this window, or with a tie
+// between a history value and a 16-bit value at the decision, go to the
+// cluster kernel.
+// ===========================================================================
+constexpr int NBIN = 16384;            // 16-bit keys counted below tau (every positive value below a tau <= 2)
+constexpr int SLOTS = NBIN / NCT;      // keys per thread range of the scan (<= NCT)
+static_assert(SLOTS <= NCT, "one key per thread inside a range");
+constexpr int HL_MAX = 64;             // history entries whose value lies in one key's cell
+constexpr int DCH = 4;                 // K4: 16-byte chunks a thread loads at a time (DCH * 8 <= 32)
+constexpr int kDeepStaticSmem = 4096;  // bound on K4's static shared memory (scan buffer, control)
+
+__device__ __forceinline__ uint32_t key16_of_bits(uint32_t u) { return (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u); }
+__device__ __forceinline__ uint32_t bits_of_key16(uint32_t k) { return (k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu); }
+template <int DT>
+__device__ __forceinline__ float val16(uint32_t k) {
+    const uint32_t b = bits_of_key16(k);
+    if constexpr (DT == FG_DTYPE_BF16) return __uint_as_float(b << 16);
+    else return __half2float(__ushort_as_half((unsigned short)b));
+}
+// Largest key whose value is <= x (strict: < x).
+template <int DT, bool STRICT>
+__device__ __forceinline__ int key16_floor(float x) {
+    uint32_t b;
+    if constexpr (DT == FG_DTYPE_BF16) b = __bfloat16_as_ushort(__float2bfloat16_rd(x));
+    else b = __half_as_ushort(__float2half_rd(x));
+    int k = (int)key16_of_bits(b);
+    while (k >= 0 && (STRICT ? !(val16<DT>((uint32_t)k) < x) : !(val16<DT>((uint32_t)k) <= x))) --k;
+    return k;
+}
+
+struct DeepCtl {
+    int flag;                 // 1: the row goes to the cluster kernel
+    int found;                // the scan found its unit / the column pass its column
+    int ut;                   // unit: 0 = a 16-bit value (slot), 1 = a history entry
+    int slot;                 // unit slot (key - klo)
+    uint32_t col;             // history entry column / found column
+    uint32_t nh;              // history entries gathered for the walk
+    uint32_t nat;             // elements of the unit
+    uint32_t owner;           // thread whose keys hold the target
+    unsigned long long before, q, base;
+    unsigned long long rem;   // the target's remainder inside the found key's cell
+};
+struct HEnt { float v; uint32_t c; };
+
+// Exclusive scan of v over the consumer threads in descending thread order
+// (thread NCT-1 first); returns the exclusive prefix, *total the sum.
+__device__ __forceinline__ unsigned long long c_scan_desc_u64(unsigned long long v, const Sm& s, unsigned long long* total) {
+    const int q = NCT - 1 - (int)threadIdx.x;          // position in the descending order
+    __shared__ unsigned long long xch[NCT];
+    xch[q] = v;
+    csync();
+    const unsigned long long w = xch[threadIdx.x];     // the value at position threadIdx.x
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const unsigned long long incl = warp_incl_scan_u64(w, lane);
+    if (lane == 31) s.ctl->red64[wid] = incl;
+    csync();
+    unsigned long long off = 0, tot = 0;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) { const unsigned long long t = s.ctl->red64[i]; if (i < wid) off += t; tot += t; }
+    xch[threadIdx.x] = off + incl - w;                 // exclusive prefix of position threadIdx.x
+    csync();
+    const unsigned long long ex = xch[q];
+    csync();
+    *total = tot;
+    return ex;
+}
+
+// Draw among the candidates (all of them kept: the cut lies below them) with
+// target Dt: the candidates' y-keys are in s.ckey (0: not a candidate).
+__device__ __noinline__ int64_t cand_draw(const Sm& s, uint32_t n, float My, float scale, uint64_t Dt, uint32_t ylo,
+                                          uint32_t yhi) {
+    const int tid = threadIdx.x;
+    auto qm = [&](uint32_t yk) -> uint64_t { return qmass(funkey(yk), My, scale); };
+    const Sel so = c_select<true>(s, [&](auto&& f) {
+        for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+            const uint32_t i = i0 + tid;
+            const uint32_t yk = i < n ? s.ckey[i] : 0u;
+            const bool v = i < n && yk != 0u;
+            f(v, yk, v ? qm(yk) : 0ull);
+        }
+    }, Dt, ylo, yhi);
+    if (!so.ok) return -1;
+    const uint32_t dkey = so.key;
+    const uint64_t qd = so.nat ? so.at / so.nat : 0;
+    const uint64_t dj = qd ? (Dt - so.before) / qd : 0;
+    uint32_t cmin = 0xffffffffu, cmax = 0u;
+    for (uint32_t i = tid; i < n; i += NCT)
+        if (s.ckey[i] == dkey) { const uint32_t kc = ~s.ccol[i]; cmin = min(cmin, kc); cmax = max(cmax, kc); }
+    c_minmax_u32(cmin, cmax, s);
+    const Sel sc = c_select<false>(s, [&](auto&& f) {
+        for (uint32_t i0 = 0; i0 < n; i0 += NCT) {
+            const uint32_t i = i0 + tid;
+            const bool v = i < n && s.ckey[i] == dkey;
+            f(v, v ? ~s.ccol[i] : 0u, 1ull);
+        }
+    }, dj, cmin, cmax);
+    if (!sc.ok) return -1;
+    return (int64_t)(~sc.key);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Params P) {
+    using E = Elem<DT>;
+    constexpr int VEC = E::VEC;
+    const Sm s = carve(P);
+    const int tid = threadIdx.x;
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(ssmem + P.off_cnt);
+    unsigned long long* tsum = reinterpret_cast<unsigned long long*>(ssmem + P.off_tsum);
+    unsigned long long* hmass = tsum + NCT;   // SLOTS entries after the NCT range sums
+    HEnt* hl = reinterpret_cast<HEnt*>(ssmem + P.off_hl);
+    __shared__ DeepCtl dc;
+    for (int r = blockIdx.x; r < P.batch; r += gridDim.x) {
+        if (__ldcg(P.out_ids + r) != kDeepId) continue;
+        const bool has_hist = P.pen_possible && (__ldg(P.hist_offsets + r + 1) > __ldg(P.hist_offsets + r));
+        const RowP p = load_row_params(P.temperature, P.top_p, P.top_k, P.rep, P.pres, P.freq, P.greedy, P.uniforms,
+                                       r, has_hist, P.vocab);
+        const RowStat rs = *row_stat(P, r);
+        const float scale = __uint_as_float((uint32_t)(127 + P.mass_shift) << 23);
+        const float M = rs.mfin, My = ydiv(p, M);
+        const float tau = rs.tau;
+        const uint64_t AC = rs.ac;
+        int status = p.bad;
+        uint32_t U = 0;
+        const uint32_t* hc = nullptr;
+        const float* hp = nullptr;
+        if (p.pen) {
+            const HistHdr* hh = hist_hdr(P, r);
+            status |= (int)hh->flags;
+            U = min(hh->nh, (uint32_t)P.hu_cap);
+            hc = g_hcol(P, r);
+            hp = g_hpen(P, r);
+        }
+        const Geom g = row_geom<E::SIZE>(P.logits, P.row_stride, P.vocab, r);
+        const int ktop = key16_floor<DT, true>(tau);    // largest key below tau
+        const int klo = ktop - (NBIN - 1);              // may be negative: those bins stay empty
+        // ---- bitmap of the history columns; counters cleared ----
+        if (P.pen_possible)
+            for (int i = tid; i <= P.nwords; i += NCT) s.hbm[i] = 0u;
+        for (int i = tid; i < NBIN; i += NCT) cnt[i] = 0u;
+        for (int i = tid; i < NCT; i += NCT) tsum[i] = 0ull;
+        if (tid == 0) { dc.flag = ktop < 0 ? 1 : 0; dc.found = 0; dc.nh = 0u; s.ctl->ovf = 0u; }
+        csync();
+        for (uint32_t i = tid; i < U; i += NCT) {
+            const uint32_t c = __ldcg(hc + i);
+            atomicOr(&s.hbm[c >> 5], 1u << (c & 31u));
+        }
+        csync();
+        // ---- pass 1: counts of the non-history 16-bit values below tau ----
+        auto count_elem = [&](uint32_t bits16) {
+            const int k = (int)key16_of_bits(bits16) - klo;
+            if (k >= 0 && k < NBIN) {
+                // the key is below tau iff its value is (keys are order-preserving)
+                if (k + klo <= ktop) atomicAdd(&cnt[k], 1u);
+            }
+        };
+        const int64_t nchunks = g.ibytes / 16;
+        const uint4* gin = reinterpret_cast<const uint4*>(g.interior);
+        for (int64_t base = 0; base < nchunks; base += DCH * NCT) {
+            uint4 v[DCH];
+#pragma unroll
+            for (int j = 0; j < DCH; ++j) {   // every load in flight before the counting
+                const int64_t ch = base + j * NCT + tid;
+                v[j] = ch < nchunks ? __ldg(gin + ch) : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int j = 0; j < DCH; ++j) {
+                const int64_t ch = base + j * NCT + tid;
+                if (ch >= nchunks) continue;
+                const int c0 = g.head + (int)ch * VEC;
+                const uint32_t hb = p.pen ? hist_bits<VEC>(s.hbm, (uint32_t)c0) : 0u;
+                const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) {
+                    if ((hb >> e) & 1u) continue;
+                    count_elem((w[e >> 1] >> (16 * (e & 1))) & 0xffffu);
+                }
+            }
+        }
+        {
+            const int nh = g.head, ntl = P.vocab - g.tail0;
+            for (int i = tid; i < nh + ntl; i += NCT) {
+                const int c = i < nh ? i : g.tail0 + (i - nh);
+                if (p.pen && hist_bit(s.hbm, (uint32_t)c)) continue;
+                count_elem(reinterpret_cast<const uint16_t*>(g.row)[c]);
+            }
+        }
+        csync();
+        // ---- masses per thread's keys (descending order: thread NCT-1 holds the largest) ----
+        // keys interleaved over the threads (populated keys come in runs), each
+        // key's mass added to the sum of its range of SLOTS keys
+        for (int k = tid; k < NBIN; k += NCT) {
+            const uint32_t c = cnt[k];
+            if (c) atomicAdd(&tsum[k / SLOTS],
+                             (unsigned long long)c * qmass(ydiv(p, val16<DT>((uint32_t)(k + klo))), My, scale));
+        }
+        // history entries below tau, each with its own mass, at the key just below or at its value
+        for (uint32_t i = tid; i < U; i += NCT) {
+            const float v = hp[i];
+            if (!(v < tau)) continue;
+            const int k = key16_floor<DT, false>(v) - klo;
+            if (k < 0) continue;   // below the window
+            atomicAdd(&tsum[k / SLOTS], qmass(ydiv(p, v), My, scale));
+        }
+        csync();
+        // ---- find: the unit at which the cumulative mass below tau passes `target` ----
+        // returns false (and flags the row) when it lies below the window
+        auto find = [&](uint64_t target) -> bool {
+            unsigned long long total = 0;
+            const unsigned long long ex = c_scan_desc_u64(tsum[tid], s, &total);
+            if (tid == 0) { dc.found = 0; dc.nh = 0u; }
+            csync();
+            if (target < total && ex <= target && target < ex + tsum[tid]) { dc.owner = (uint32_t)tid; dc.base = ex; }
+            csync();
+            if (!(target < total)) { if (tid == 0) dc.flag = 1; csync(); return false; }
+            const int own = (int)dc.owner;
+            const int k0 = own * SLOTS;
+            // per key of the owner's range: the history entries in its cell [value(k), value(k+1))
+            for (int j = tid; j < SLOTS; j += NCT) { hmass[j] = 0ull; }
+            csync();
+            for (uint32_t i = tid; i < U; i += NCT) {
+                const float v = hp[i];
+                if (!(v < tau)) continue;
+                const int k = key16_floor<DT, false>(v) - klo;
+                if (k < k0 || k >= k0 + SLOTS) continue;
+                atomicAdd(&hmass[k - k0], qmass(ydiv(p, v), My, scale));
+            }
+            csync();
+            // one key per thread, threads NCT-SLOTS.. NCT-1 in ascending key order, so the
+            // descending scan visits the keys from the largest down
+            const int j = tid - (NCT - SLOTS);
+            unsigned long long mk = 0;
+            uint64_t qk = 0;
+            if (j >= 0) {
+                const uint32_t c = cnt[k0 + j];
+                if (c) qk = qmass(ydiv(p, val16<DT>((uint32_t)(k0 + j + klo))), My, scale);
+                mk = hmass[j] + (unsigned long long)c * qk;
+            }
+            unsigned long long tot2 = 0;
+            const unsigned long long ex2 = c_scan_desc_u64(mk, s, &tot2);
+            const uint64_t rem = target - dc.base;   // dc.base is not written in this step
+            if (j >= 0 && ex2 <= rem && rem < ex2 + mk) {
+                dc.slot = k0 + j;
+                dc.before = AC + dc.base + ex2;   // mass before the key's cell
+                dc.rem = rem - ex2;
+            }
+            csync();
+            const int ks = dc.slot;
+            // the cell's history entries (largest first), then the key's own elements
+            for (uint32_t i = tid; i < U; i += NCT) {
+                const float v = hp[i];
+                if (!(v < tau)) continue;
+                if (key16_floor<DT, false>(v) - klo != ks) continue;
+                const uint32_t pos = atomicAdd(&dc.nh, 1u);
+                if (pos < (uint32_t)HL_MAX) { hl[pos].v = v; hl[pos].c = __ldcg(hc + i); }
+            }
+            csync();
+            if (tid == 0) {
+                const uint32_t nh = dc.nh;
+                if (nh > (uint32_t)HL_MAX) {
+                    dc.flag = 1;
+                } else {
+                    // descending value, ascending column
+                    for (uint32_t a = 1; a < nh; ++a) {
+                        const HEnt x = hl[a];
+                        uint32_t b = a;
+                        while (b > 0 && (hl[b - 1].v < x.v || (hl[b - 1].v == x.v && hl[b - 1].c > x.c))) { hl[b] = hl[b - 1]; --b; }
+                        hl[b] = x;
+                    }
+                    const float gy = ydiv(p, val16<DT>((uint32_t)(ks + klo)));
+                    const uint32_t c = cnt[ks];
+                    uint64_t r2 = dc.rem, before = dc.before;
+                    bool done = false;
+                    for (uint32_t h = 0; h < nh && !done; ++h) {
+                        const float hy = ydiv(p, hl[h].v);
+                        if (hy == gy && c != 0u) { dc.flag = 1; done = true; break; }   // a tie across kinds
+                        const uint64_t qh = qmass(hy, My, scale);
+                        if (r2 < qh) {
+                            dc.ut = 1; dc.col = hl[h].c; dc.nat = 1; dc.q = qh; dc.before = before;
+                            dc.found = 1; done = true;
+                        } else {
+                            r2 -= qh; before += qh;
+                        }
+                    }
+                    if (!done) {
+                        const uint64_t q = qmass(gy, My, scale);
+                        if (c == 0u || r2 >= (uint64_t)c * q) {
+                            dc.flag = 1;   // rounding put the target past the cell: leave the row
+                        } else if ((ks + klo < ktop && ydiv(p, val16<DT>((uint32_t)(ks + klo + 1))) == gy) ||
+                                   (ks + klo > 0 && ydiv(p, val16<DT>((uint32_t)(ks + klo - 1))) == gy)) {
+                            dc.flag = 1;   // equal y on a neighbouring 16-bit value would interleave columns
+                        } else {
+                            dc.ut = 0; dc.nat = c; dc.q = q; dc.before = before; dc.found = 1;
+                        }
+                    }
+                }
+            }
+            csync();
+            return dc.flag == 0 && dc.found != 0;
+        };
+        // ---- the j-th (ascending) non-history column with key (slot + klo) ----
+        auto column = [&](int slot, uint64_t j) -> int64_t {
+            const uint32_t kk = (uint32_t)(slot + klo);
+            if (tid == 0) { dc.found = 0; dc.base = 0; }
+            csync();
+            auto match = [&](int c, uint32_t bits16) {
+                return key16_of_bits(bits16) == kk && !(p.pen && hist_bit(s.hbm, (uint32_t)c));
+            };
+            // ragged head first (thread 0), then the interior a tile of NCT chunks at a time, then the tail
+            if (tid == 0) {
+                uint64_t run = 0;
+                for (int c = 0; c < g.head; ++c)
+                    if (match(c, reinterpret_cast<const uint16_t*>(g.row)[c])) {
+                        if (run == j) { dc.found = 1; dc.col = (uint32_t)c; break; }
+                        ++run;
+                    }
+                dc.base = run;
+            }
+            csync();
+            for (int64_t t0 = 0; t0 < nchunks && !dc.found; t0 += DCH * NCT) {
+                // thread tid holds the DCH consecutive chunks from ch0: a scan in
+                // thread order is a scan in column order
+                const int64_t ch0 = t0 + (int64_t)tid * DCH;
+                uint4 v[DCH];
+#pragma unroll
+                for (int j = 0; j < DCH; ++j)
+                    v[j] = ch0 + j < nchunks ? __ldg(gin + ch0 + j) : make_uint4(0u, 0u, 0u, 0u);
+                uint32_t m = 0u, mm = 0u;   // matches; bit j*VEC+e of mm (DCH * VEC <= 32)
+#pragma unroll
+                for (int j = 0; j < DCH; ++j) {
+                    if (ch0 + j >= nchunks) continue;
+                    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+                    const int c0 = g.head + (int)(ch0 + j) * VEC;
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e)
+                        if (match(c0 + e, (w[e >> 1] >> (16 * (e & 1))) & 0xffffu)) { mm |= 1u << (j * VEC + e); ++m; }
+                }
+                // exclusive scan of m in thread order
+                const int lane = tid & 31, wid = tid >> 5;
+                const uint32_t incl = warp_incl_scan_u32(m, lane);
+                if (lane == 31) s.ctl->red32[wid] = incl;
+                csync();
+                uint32_t off = 0, tot = 0;
+#pragma unroll
+                for (int i = 0; i < NCW; ++i) { const uint32_t t = s.ctl->red32[i]; if (i < wid) off += t; tot += t; }
+                const uint64_t b0 = dc.base + off + incl - m;
+                if (m && b0 <= j && j < b0 + m) {
+                    uint32_t left = (uint32_t)(j - b0), bits = mm;
+                    while (left--) bits &= bits - 1u;
+                    dc.col = (uint32_t)(g.head + (int)ch0 * VEC + (__ffs(bits) - 1));
+                    dc.found = 1;
+                }
+                csync();
+                if (tid == 0) dc.base += tot;
+                csync();
+            }
+            if (tid == 0 && !dc.found) {
+                uint64_t run = dc.base;
+                for (int c = g.tail0; c < P.vocab; ++c)
+                    if (match(c, reinterpret_cast<const uint16_t*>(g.row)[c])) {
+                        if (run == j) { dc.found = 1; dc.col = (uint32_t)c; break; }
+                        ++run;
+                    }
+            }
+            csync();
+            const int64_t res = dc.found ? (int64_t)dc.col : -1;
+            csync();
+            return res;
+        };
+        // ---- the cut, then the draw ----
+        int64_t out = -1;
+        bool defer = dc.flag != 0;
+        const double Zq = rs.zq;
+        uint64_t Qf = 0, before_t = 0, qt = 0;
+        int cut_ut = -1, cut_slot = 0;
+        uint32_t cut_col = 0;
+        bool cut = false;
+        if (!defer && p.use_p) {
+            const uint64_t Pt = (uint64_t)floor((double)p.top_p * Zq);
+            if (Pt < AC || !find(Pt - AC)) {
+                defer = true;
+            } else {
+                cut = true; cut_ut = dc.ut; cut_slot = dc.slot; cut_col = dc.col;
+                before_t = dc.before; qt = dc.q;
+                uint64_t m = dc.nat;
+                if (qt > 0) { const uint64_t mm = (Pt - before_t) / qt + 1; if (mm < m) m = mm; }
+                Qf = before_t + m * qt;
+            }
+        } else if (!defer) {
+            Qf = (uint64_t)Zq;
+        }
+        if (!defer && Qf == 0) defer = true;
+        if (!defer) {
+            uint64_t Dt = (uint64_t)floor((double)p.u * (double)Qf);
+            if (Dt >= Qf) Dt = Qf - 1;
+            if (cut && Dt >= before_t) {
+                const uint64_t dj = qt ? (Dt - before_t) / qt : 0;
+                out = cut_ut == 1 ? (int64_t)cut_col : column(cut_slot, dj);
+            } else if (Dt < AC) {
+                // among the candidates: their y-keys, then the select
+                const uint32_t n = min(rs.n, (uint32_t)P.cap);
+                const uint32_t* gk = g_ckey(P, r);
+                const uint32_t* gc = g_ccol(P, r);
+                const uint32_t ktau = fkey(tau);
+                uint32_t ylo = 0xffffffffu, yhi = 0u;
+                for (uint32_t i = tid; i < n; i += NCT) {
+                    const uint32_t k = gk[i];
+                    uint32_t yk = 0u;
+                    if (k >= ktau) { yk = fkey(ydiv(p, funkey(k))); ylo = min(ylo, yk); yhi = max(yhi, yk); }
+                    s.ckey[i] = yk; s.ccol[i] = gc[i];
+                }
+                uint32_t nn = n;
+                // the history entries at or above tau are candidates too
+                if (p.pen) {
+                    if (tid == 0) s.ctl->ncand = n;
+                    csync();
+                    for (uint32_t i = tid; i < U; i += NCT) {
+                        const float v = hp[i];
+                        if (!(v >= tau)) continue;
+                        const uint32_t pos = atomicAdd(&s.ctl->ncand, 1u);
+                        if (pos < (uint32_t)P.cap) {
+                            const uint32_t yk = fkey(ydiv(p, v));
+                            s.ckey[pos] = yk; s.ccol[pos] = __ldcg(hc + i);
+                            ylo = min(ylo, yk); yhi = max(yhi, yk);
+                        } else {
+                            s.ctl->ovf = 1u;
+                        }
+                    }
+                    csync();
+                    nn = min(s.ctl->ncand, (uint32_t)P.cap);
+                    if (s.ctl->ovf) defer = true;
+                    csync();
+                }
+                c_minmax_u32(ylo, yhi, s);
+                if (!defer) {
+                    out = cand_draw(s, nn, My, scale, Dt, ylo, yhi);
+                    if (out < 0) defer = true;
+                }
+            } else if (find(Dt - AC)) {
+                const uint64_t dj = dc.q ? (Dt - dc.before) / dc.q : 0;
+                out = dc.ut == 1 ? (int64_t)dc.col : column(dc.slot, dj);
+            } else {
+                defer = true;
+            }
+            if (out < 0) defer = true;
+        }
+        if (tid == 0) {
+            if (defer) {
+                P.out_ids[r] = kDeferredId;
+            } else {
+                P.out_ids[r] = out + P.vocab_offset;
                 if (P.out_status) P.out_status[r] = status;
             }
         }

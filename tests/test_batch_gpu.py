@@ -1,0 +1,81 @@
+"""Parity of the batch path (history prep, stream, decide, and the 16-bit
+deep-nucleus finish) with the CPU oracle. Batches here are large enough that
+fg_sample takes the batch path rather than one cluster per row, and no
+kept-set probabilities are requested (a call that wants them is sampled by the
+cluster kernel), so the ids compared are the batch path's own.
+
+Token ids must be identical on every row the oracle does not flag as within
+1e-6 of a CDF or top-p boundary (reference: flashgen/sampling/sampler.py:57-169,
+draw order of csrc/runtime/pipeline.cpp:311-340)."""
+import numpy as np
+import pytest
+import torch
+
+from flashgen_b200 import _lib
+from flashgen_b200.workloads import BatchParams, Workload, make_workload
+from oracle import sampler_oracle as O
+from tests.gpu_helpers import compare, run_kernel
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle(w):
+    return O.sample_rows(w.logits, w.params, w.histories(), w.uniforms, stable=True)
+
+
+@pytest.mark.parametrize("cfg,batch", [(2, 256), (3, 256), (4, 192)])
+def test_batch_path_configs(cuda_device, cfg, batch):
+    w = make_workload(cfg, batch=batch, seed=21)
+    ids, status, _ = run_kernel(w, probs=False)
+    stats = compare(w, _oracle(w), ids, status, None)
+    print(f"cfg{cfg}", stats)
+    # the batch path decided most rows itself
+    assert stats["general_path"] <= batch // 4, stats
+
+
+def test_config3_every_row(cuda_device):
+    """Configuration 3 at its full size: every one of the 1024 rows against the
+    oracle, with the flagged-row and tie counts printed."""
+    w = make_workload(3, seed=11)
+    ids, status, _ = run_kernel(w, probs=False)
+    res = _oracle(w)
+    stats = compare(w, res, ids, status, None)
+    stats["tie_at_cut"] = int(res.tie_at_cut.sum())
+    print("cfg3 full", stats)
+
+
+def _deep_workload(dtype, B, V, hist, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((B, V), dtype=np.float32)
+    for r in range(B):
+        x[r, rng.choice(V, V // 100, replace=False)] += 6.0
+    p = BatchParams.uniform(B)
+    p.temperature[:] = rng.uniform(0.6, 1.2, B).astype(np.float32)
+    p.top_k[:] = 0
+    # cuts and draws among the positive values below the candidates (a cut in
+    # the negative values of these rows may be handed to the cluster kernel)
+    p.top_p[:] = rng.choice(np.array([0.85, 0.88, 0.9, 0.92, 0.95], np.float32), B)
+    rows = [np.zeros(0, np.int32)] * B
+    if hist:
+        p.repetition_penalty[:] = rng.uniform(1.0, 1.3, B).astype(np.float32)
+        p.presence_penalty[:] = rng.uniform(0.0, 0.4, B).astype(np.float32)
+        p.frequency_penalty[:] = rng.uniform(0.0, 0.2, B).astype(np.float32)
+        rows = [((rng.zipf(1.1, 512) - 1) % V).astype(np.int32) for _ in range(B)]
+    offs = np.zeros(B + 1, np.int64)
+    offs[1:] = np.cumsum([len(h) for h in rows])
+    ids = np.concatenate(rows).astype(np.int32) if offs[-1] else np.zeros(0, np.int32)
+    u = rng.random(B, dtype=np.float32)
+    return Workload(0, "deep", torch.from_numpy(x).to(dtype), p, ids, offs, u)
+
+
+@pytest.mark.parametrize("hist", [False, True])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_deep_nucleus_16bit(cuda_device, dtype, hist):
+    """Top-p cuts and draws below the candidate set: the 16-bit finish counts
+    the row's values below the candidates' threshold and walks them."""
+    w = _deep_workload(dtype, 192, 32000, hist, seed=5 + int(hist))
+    ids, status, _ = run_kernel(w, probs=False)
+    stats = compare(w, _oracle(w), ids, status, None)
+    print(dtype, hist, stats)
+    # the deep rows were finished on the batch path, not handed to the cluster kernel
+    assert stats["general_path"] <= w.batch // 8, stats
