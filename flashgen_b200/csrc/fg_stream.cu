@@ -12,7 +12,7 @@ namespace host {
 
 namespace {
 
-constexpr int kCap = 4096;            // candidate entries (shared memory and row block)
+constexpr int kCap = 3072;            // candidate entries (shared memory and row block)
 constexpr int kMinStages = 3;
 
 template <class K>

@@ -1399,7 +1399,7 @@ __global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Par
 // between a history value and a 16-bit value at the decision, go to the
 // cluster kernel.
 // ===========================================================================
-constexpr int NBIN = 16384;            // 16-bit keys counted below tau (every positive value below a tau <= 2)
+constexpr int NBIN = 16384;            // slots of the 16-bit keys counted below tau
 constexpr int SLOTS = NBIN / NCT;      // keys per thread range of the scan (<= NCT)
 static_assert(SLOTS <= NCT, "one key per thread inside a range");
 constexpr int HL_MAX = 64;             // history entries whose value lies in one key's cell
@@ -1424,6 +1424,23 @@ __device__ __forceinline__ int key16_floor(float x) {
     while (k >= 0 && (STRICT ? !(val16<DT>((uint32_t)k) < x) : !(val16<DT>((uint32_t)k) <= x))) --k;
     return k;
 }
+
+// Slots of the 16-bit keys. For bf16 the 24832 keys of the values with
+// |x| < 2^-30 (both signs, zero included) share one slot, the zone: their
+// masses are equal in fp32 (e^(y - My) with |y| < 2^-29 / T), so slot sums
+// stay exact, and a target that falls inside the zone hands the row on.
+// NBIN slots below a tau of a few units then reach the most negative values.
+template <int DT>
+struct VK {
+    static constexpr bool Z = DT == FG_DTYPE_BF16;
+    static constexpr uint32_t ZLO = 0x4F7Fu;   // key of -2^-30
+    static constexpr uint32_t ZHI = 0xB080u;   // key of +2^-30
+    static constexpr uint32_t ZW = ZHI - ZLO - 1u;
+    __device__ static uint32_t of(uint32_t k) { return !Z ? k : (k >= ZHI ? k - ZW + 1u : (k > ZLO ? ZLO + 1u : k)); }
+    __device__ static bool zone(uint32_t vk) { return Z && vk == ZLO + 1u; }
+    // a key of the slot (for the zone: one of its keys, whose mass all of them share)
+    __device__ static uint32_t key(uint32_t vk) { return !Z ? vk : (vk > ZLO + 1u ? vk + ZW - 1u : vk); }
+};
 
 struct DeepCtl {
     int flag;                 // 1: the row goes to the cluster kernel
@@ -1528,7 +1545,8 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
             hp = g_hpen(P, r);
         }
         const Geom g = row_geom<E::SIZE>(P.logits, P.row_stride, P.vocab, r);
-        const int ktop = key16_floor<DT, true>(tau);    // largest key below tau
+        const int ktop_raw = key16_floor<DT, true>(tau);   // largest key below tau
+        const int ktop = ktop_raw < 0 ? -1 : (int)VK<DT>::of((uint32_t)ktop_raw);   // its slot
         const int klo = ktop - (NBIN - 1);              // may be negative: those bins stay empty
         // ---- bitmap of the history columns; counters cleared ----
         if (P.pen_possible)
@@ -1544,11 +1562,11 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
         csync();
         // ---- pass 1: counts of the non-history 16-bit values below tau ----
         auto count_elem = [&](uint32_t bits16) {
-            const int k = (int)key16_of_bits(bits16) - klo;
-            if (k >= 0 && k < NBIN) {
-                // the key is below tau iff its value is (keys are order-preserving)
-                if (k + klo <= ktop) atomicAdd(&cnt[k], 1u);
-            }
+            // below tau iff the key is (keys are order-preserving)
+            const int key = (int)key16_of_bits(bits16);
+            if (key > ktop_raw) return;
+            const int k = (int)VK<DT>::of((uint32_t)key) - klo;
+            if (k >= 0) atomicAdd(&cnt[k], 1u);
         };
         const int64_t nchunks = g.ibytes / 16;
         const uint4* gin = reinterpret_cast<const uint4*>(g.interior);
@@ -1588,13 +1606,13 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
         for (int k = tid; k < NBIN; k += NCT) {
             const uint32_t c = cnt[k];
             if (c) atomicAdd(&tsum[k / SLOTS],
-                             (unsigned long long)c * qmass(ydiv(p, val16<DT>((uint32_t)(k + klo))), My, scale));
+                             (unsigned long long)c * qmass(ydiv(p, val16<DT>(VK<DT>::key((uint32_t)(k + klo)))), My, scale));
         }
         // history entries below tau, each with its own mass, at the key just below or at its value
         for (uint32_t i = tid; i < U; i += NCT) {
             const float v = hp[i];
             if (!(v < tau)) continue;
-            const int k = key16_floor<DT, false>(v) - klo;
+            const int k = (int)VK<DT>::of((uint32_t)key16_floor<DT, false>(v)) - klo;
             if (k < 0) continue;   // below the window
             atomicAdd(&tsum[k / SLOTS], qmass(ydiv(p, v), My, scale));
         }
@@ -1617,7 +1635,7 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
             for (uint32_t i = tid; i < U; i += NCT) {
                 const float v = hp[i];
                 if (!(v < tau)) continue;
-                const int k = key16_floor<DT, false>(v) - klo;
+                const int k = (int)VK<DT>::of((uint32_t)key16_floor<DT, false>(v)) - klo;
                 if (k < k0 || k >= k0 + SLOTS) continue;
                 atomicAdd(&hmass[k - k0], qmass(ydiv(p, v), My, scale));
             }
@@ -1629,7 +1647,7 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
             uint64_t qk = 0;
             if (j >= 0) {
                 const uint32_t c = cnt[k0 + j];
-                if (c) qk = qmass(ydiv(p, val16<DT>((uint32_t)(k0 + j + klo))), My, scale);
+                if (c) qk = qmass(ydiv(p, val16<DT>(VK<DT>::key((uint32_t)(k0 + j + klo)))), My, scale);
                 mk = hmass[j] + (unsigned long long)c * qk;
             }
             unsigned long long tot2 = 0;
@@ -1646,15 +1664,15 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
             for (uint32_t i = tid; i < U; i += NCT) {
                 const float v = hp[i];
                 if (!(v < tau)) continue;
-                if (key16_floor<DT, false>(v) - klo != ks) continue;
+                if ((int)VK<DT>::of((uint32_t)key16_floor<DT, false>(v)) - klo != ks) continue;
                 const uint32_t pos = atomicAdd(&dc.nh, 1u);
                 if (pos < (uint32_t)HL_MAX) { hl[pos].v = v; hl[pos].c = __ldcg(hc + i); }
             }
             csync();
             if (tid == 0) {
                 const uint32_t nh = dc.nh;
-                if (nh > (uint32_t)HL_MAX) {
-                    dc.flag = 1;
+                if (nh > (uint32_t)HL_MAX || VK<DT>::zone((uint32_t)(ks + klo))) {
+                    dc.flag = 1;   // too many entries in the cell, or the target inside the zone
                 } else {
                     // descending value, ascending column
                     for (uint32_t a = 1; a < nh; ++a) {
@@ -1663,7 +1681,7 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
                         while (b > 0 && (hl[b - 1].v < x.v || (hl[b - 1].v == x.v && hl[b - 1].c > x.c))) { hl[b] = hl[b - 1]; --b; }
                         hl[b] = x;
                     }
-                    const float gy = ydiv(p, val16<DT>((uint32_t)(ks + klo)));
+                    const float gy = ydiv(p, val16<DT>(VK<DT>::key((uint32_t)(ks + klo))));
                     const uint32_t c = cnt[ks];
                     uint64_t r2 = dc.rem, before = dc.before;
                     bool done = false;
@@ -1682,8 +1700,8 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
                         const uint64_t q = qmass(gy, My, scale);
                         if (c == 0u || r2 >= (uint64_t)c * q) {
                             dc.flag = 1;   // rounding put the target past the cell: leave the row
-                        } else if ((ks + klo < ktop && ydiv(p, val16<DT>((uint32_t)(ks + klo + 1))) == gy) ||
-                                   (ks + klo > 0 && ydiv(p, val16<DT>((uint32_t)(ks + klo - 1))) == gy)) {
+                        } else if ((ks + klo < ktop && ydiv(p, val16<DT>(VK<DT>::key((uint32_t)(ks + klo + 1)))) == gy) ||
+                                   (ks + klo > 0 && ydiv(p, val16<DT>(VK<DT>::key((uint32_t)(ks + klo - 1)))) == gy)) {
                             dc.flag = 1;   // equal y on a neighbouring 16-bit value would interleave columns
                         } else {
                             dc.ut = 0; dc.nat = c; dc.q = q; dc.before = before; dc.found = 1;
@@ -1696,7 +1714,7 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
         };
         // ---- the j-th (ascending) non-history column with key (slot + klo) ----
         auto column = [&](int slot, uint64_t j) -> int64_t {
-            const uint32_t kk = (uint32_t)(slot + klo);
+            const uint32_t kk = VK<DT>::key((uint32_t)(slot + klo));   // never the zone (it defers)
             if (tid == 0) { dc.found = 0; dc.base = 0; }
             csync();
             auto match = [&](int c, uint32_t bits16) {

@@ -44,7 +44,7 @@ def test_config3_every_row(cuda_device):
     print("cfg3 full", stats)
 
 
-def _deep_workload(dtype, B, V, hist, seed):
+def _deep_workload(dtype, B, V, hist, seed, top_ps=(0.85, 0.88, 0.9, 0.92, 0.95)):
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((B, V), dtype=np.float32)
     for r in range(B):
@@ -52,9 +52,7 @@ def _deep_workload(dtype, B, V, hist, seed):
     p = BatchParams.uniform(B)
     p.temperature[:] = rng.uniform(0.6, 1.2, B).astype(np.float32)
     p.top_k[:] = 0
-    # cuts and draws among the positive values below the candidates (a cut in
-    # the negative values of these rows may be handed to the cluster kernel)
-    p.top_p[:] = rng.choice(np.array([0.85, 0.88, 0.9, 0.92, 0.95], np.float32), B)
+    p.top_p[:] = rng.choice(np.array(top_ps, np.float32), B)
     rows = [np.zeros(0, np.int32)] * B
     if hist:
         p.repetition_penalty[:] = rng.uniform(1.0, 1.3, B).astype(np.float32)
@@ -79,3 +77,13 @@ def test_deep_nucleus_16bit(cuda_device, dtype, hist):
     print(dtype, hist, stats)
     # the deep rows were finished on the batch path, not handed to the cluster kernel
     assert stats["general_path"] <= w.batch // 8, stats
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_deep_nucleus_16bit_tail(cuda_device, dtype):
+    """Nuclei reaching the negative values of the row (top-p near 1) and rows
+    with top-p 1 (a draw over the whole row)."""
+    w = _deep_workload(dtype, 192, 32000, True, seed=9, top_ps=(0.97, 0.99, 0.995, 0.999, 1.0))
+    ids, status, _ = run_kernel(w, probs=False)
+    stats = compare(w, _oracle(w), ids, status, None)
+    print(dtype, "tail", stats)
