@@ -104,6 +104,15 @@ class Workload:
             return 0
         return int(np.diff(self.hist_offsets).max(initial=0))
 
+    def rows(self, lo: int, hi: int) -> "Workload":
+        """Rows [lo, hi) as a workload of their own (a rank's block of a
+        row-sharded batch); the history CSR is rebased."""
+        o = self.hist_offsets
+        ids = self.hist_ids[o[lo]:o[hi]]
+        offs = (o[lo:hi + 1] - o[lo]).astype(np.int64)
+        return Workload(self.config, self.name, self.logits[lo:hi], self.params.slice(lo, hi), ids, offs,
+                        self.uniforms[lo:hi])
+
     def algorithmic_bytes(self) -> int:
         """Bytes one sampling step must move: logits + histories + per-row
         params (7 fields), uniform, id and offsets."""

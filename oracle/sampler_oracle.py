@@ -257,3 +257,55 @@ def repetition_penalty_inplace(logits: torch.Tensor,
         v = logits[i, uid]
         logits[i, uid] = torch.where(v > 0, v / pen, v * pen)
     return logits
+
+
+def reference_chain_rows(logits: torch.Tensor, params: RowParams,
+                         histories: Optional[Sequence[Sequence[int]]],
+                         generator: Optional[torch.Generator] = None) -> np.ndarray:
+    """The reference's own CPU sampling path, timed as the CPU baseline.
+
+    The torch operations of FlashGen's decode step in the reference's order,
+    without this module's parity flags, float64 cut and kept sets:
+    ``Sampler.apply_repetition_penalty`` (sampler.py:123-147, unique history
+    ids), then ``Sampler.sample`` (sampler.py:57-88): the all-greedy fast path
+    (argmax of the batch), else per row argmax (greedy) or ``_sample_one``
+    (sampler.py:102-121): ``x / T``, ``_top_k_filter``, ``_top_p_filter``
+    (torch's default sort, sampler.py:156-169), softmax and
+    ``torch.multinomial``. Presence and frequency penalties are absent from
+    the reference and are not applied here.
+    """
+    B, V = logits.shape
+    x = logits.to(torch.float32).clone()
+    if histories is not None:
+        for i in range(B):
+            pen = float(params.repetition_penalty[i])
+            if pen == 1.0 or len(histories[i]) == 0:
+                continue
+            uid = torch.as_tensor(np.asarray(histories[i], dtype=np.int64)).unique()
+            v = x[i, uid]
+            x[i, uid] = torch.where(v > 0, v / pen, v * pen)
+    greedy = [bool(params.greedy[i]) or float(params.temperature[i]) == 0.0 for i in range(B)]
+    if all(greedy):
+        return x.argmax(dim=-1).numpy()
+    out = np.empty(B, dtype=np.int64)
+    for i in range(B):
+        logit = x[i]
+        if greedy[i]:
+            out[i] = int(logit.argmax())
+            continue
+        T = float(params.temperature[i])
+        if T != 1.0 and T > 0:
+            logit = logit / T
+        k = int(params.top_k[i])
+        if k > 0:
+            logit = top_k_filter(logit, k)
+        p = float(params.top_p[i])
+        if 0.0 < p < 1.0:
+            sl, si = logit.sort(descending=True)
+            cp = F.softmax(sl, dim=-1).cumsum(dim=-1)
+            remove = cp - F.softmax(sl, dim=-1) > p
+            sl = sl.masked_fill(remove, float("-inf"))
+            logit = logit.scatter(0, si, sl)
+        probs = F.softmax(logit, dim=-1)
+        out[i] = int(torch.multinomial(probs.unsqueeze(0), 1, generator=generator).squeeze())
+    return out
