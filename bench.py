@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--latency-steps", type=int, default=10000)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0, help="rows of the timed batch (default: the configuration's)")
+    ap.add_argument("--only-step", action="store_true",
+                    help="time the fg_sample step alone (no other legs): the command the ncu captures use")
     return ap.parse_args()
 
 
@@ -507,8 +510,8 @@ def main():
     _lib.load(build_if_missing=False)
     cfg = args.config
     # one global batch (same seed on every rank); rank g samples its row block
-    wfull = make_workload(cfg, seed=1)
-    wfull2 = make_workload(cfg, seed=2)
+    wfull = make_workload(cfg, seed=1, batch=args.batch or None)
+    wfull2 = make_workload(cfg, seed=2, batch=args.batch or None)
     Bg, V = wfull.batch, wfull.vocab
     if Bg % world:
         raise SystemExit(f"batch {Bg} is not a multiple of {world}")
@@ -556,6 +559,15 @@ def main():
     general_rows = int(((st0 & _lib.FG_ROW_GENERAL_PATH) != 0).sum())
     del bt
     torch.cuda.empty_cache()
+
+    if args.only_step:
+        if rank == 0:
+            print(json.dumps({"metric": "sampled_rows_per_s", "value": rows_s, "unit": "rows/s", "n_gpus": world,
+                              "steps": args.steps, "ms_per_step": ms / args.steps, "batch": Bg,
+                              "workload": CONFIG_NAMES[cfg], "general_path_rows": general_rows}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
 
     # ---- weak scaling: every rank samples a full batch of its own ----
     weak = None
