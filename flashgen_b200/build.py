@@ -1,6 +1,7 @@
 """Build the sampler's C-ABI shared library for sm_100a (in tree).
 
     python -m flashgen_b200.build          # -> flashgen_b200/lib/libflashgen_sampler.so
+                                           #    flashgen_b200/_C*.so (PyBind11 binding)
 
 The library is plain nvcc output (``-shared``, static CUDA runtime) so that it
 has no torch dependency and loads through ctypes, cgo, JNI or pybind11 alike.
@@ -26,6 +27,8 @@ SOURCES = [os.path.join(CSRC, f) for f in ("fg_abi.cu", "fg_host.cu", "fg_cluste
 HEADERS = sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))) + [
     os.path.join(ROOT, "include", "flashgen_sampler.h")]
 DEPS = SOURCES + HEADERS
+
+BINDINGS = os.path.join(CSRC, "bindings", "fg_bindings.cpp")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v"]
@@ -98,5 +101,31 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIBPATH
 
 
+def bindings_path() -> str:
+    import sysconfig
+    return os.path.join(HERE, "_C" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_bindings(force: bool = False) -> str:
+    """The PyBind11 module flashgen_b200._C, linked against the in-tree
+    library (found through an $ORIGIN-relative rpath)."""
+    import sysconfig
+    import pybind11
+    out = bindings_path()
+    deps = [BINDINGS, os.path.join(ROOT, "include", "flashgen_sampler.h"), LIBPATH]
+    if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps):
+        return out
+    cxx = shutil.which("g++") or "g++"
+    cmd = [cxx, "-O2", "-shared", "-fPIC", "-std=c++17", "-fvisibility=hidden",
+           "-I", pybind11.get_include(), "-I", sysconfig.get_paths()["include"],
+           BINDINGS, "-o", out + ".tmp", "-L", LIBDIR, "-lflashgen_sampler", "-Wl,-rpath,$ORIGIN/lib"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("bindings build failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+    os.replace(out + ".tmp", out)
+    return out
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose=True))
+    print(build_bindings(force="--force" in sys.argv))

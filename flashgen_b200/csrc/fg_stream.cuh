@@ -1403,7 +1403,7 @@ constexpr int NBIN = 16384;            // slots of the 16-bit keys counted below
 constexpr int SLOTS = NBIN / NCT;      // keys per thread range of the scan (<= NCT)
 static_assert(SLOTS <= NCT, "one key per thread inside a range");
 constexpr int HL_MAX = 64;             // history entries whose value lies in one key's cell
-constexpr int DCH = 4;                 // K4: 16-byte chunks a thread loads at a time (DCH * 8 <= 32)
+constexpr int DCH = 8;                 // K4: 16-byte chunks a thread loads at a time (DCH * VEC <= 64)
 constexpr int kDeepStaticSmem = 4096;  // bound on K4's static shared memory (scan buffer, control)
 
 __device__ __forceinline__ uint32_t key16_of_bits(uint32_t u) { return (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u); }
@@ -1739,7 +1739,8 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
 #pragma unroll
                 for (int j = 0; j < DCH; ++j)
                     v[j] = ch0 + j < nchunks ? __ldg(gin + ch0 + j) : make_uint4(0u, 0u, 0u, 0u);
-                uint32_t m = 0u, mm = 0u;   // matches; bit j*VEC+e of mm (DCH * VEC <= 32)
+                uint32_t m = 0u;
+                unsigned long long mm = 0ull;   // matches; bit j*VEC+e of mm (DCH * VEC <= 64)
 #pragma unroll
                 for (int j = 0; j < DCH; ++j) {
                     if (ch0 + j >= nchunks) continue;
@@ -1747,7 +1748,7 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
                     const int c0 = g.head + (int)(ch0 + j) * VEC;
 #pragma unroll
                     for (int e = 0; e < VEC; ++e)
-                        if (match(c0 + e, (w[e >> 1] >> (16 * (e & 1))) & 0xffffu)) { mm |= 1u << (j * VEC + e); ++m; }
+                        if (match(c0 + e, (w[e >> 1] >> (16 * (e & 1))) & 0xffffu)) { mm |= 1ull << (j * VEC + e); ++m; }
                 }
                 // exclusive scan of m in thread order
                 const int lane = tid & 31, wid = tid >> 5;
@@ -1759,9 +1760,10 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
                 for (int i = 0; i < NCW; ++i) { const uint32_t t = s.ctl->red32[i]; if (i < wid) off += t; tot += t; }
                 const uint64_t b0 = dc.base + off + incl - m;
                 if (m && b0 <= j && j < b0 + m) {
-                    uint32_t left = (uint32_t)(j - b0), bits = mm;
-                    while (left--) bits &= bits - 1u;
-                    dc.col = (uint32_t)(g.head + (int)ch0 * VEC + (__ffs(bits) - 1));
+                    uint32_t left = (uint32_t)(j - b0);
+                    unsigned long long bits = mm;
+                    while (left--) bits &= bits - 1ull;
+                    dc.col = (uint32_t)(g.head + (int)ch0 * VEC + (__ffsll((long long)bits) - 1));
                     dc.found = 1;
                 }
                 csync();

@@ -87,3 +87,36 @@ def test_deep_nucleus_16bit_tail(cuda_device, dtype):
     ids, status, _ = run_kernel(w, probs=False)
     stats = compare(w, _oracle(w), ids, status, None)
     print(dtype, "tail", stats)
+
+
+def test_pybind_sample_matches_oracle(cuda_device):
+    """fg_sample through the PyBind11 module (_C.sample, GIL released) on
+    configuration 2 rows, against the oracle."""
+    import importlib
+
+    from flashgen_b200 import build as _build
+    from flashgen_b200.sampling.sampler import PackedParams, workspace_for
+
+    _build.build_bindings()
+    C = importlib.import_module("flashgen_b200._C")
+    dev = cuda_device
+    w = make_workload(2, batch=96, seed=4)
+    p = w.params
+    packed = PackedParams(p.temperature, p.top_p, p.top_k, p.repetition_penalty, p.presence_penalty,
+                          p.frequency_penalty, p.greedy, dev)
+    lg = w.logits.to(dev)
+    u = torch.from_numpy(w.uniforms).to(dev)
+    hid, hoff = torch.from_numpy(w.hist_ids).to(dev), torch.from_numpy(w.hist_offsets).to(dev)
+    out = torch.empty(w.batch, dtype=torch.int64, device=dev)
+    status = torch.empty(w.batch, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ws = workspace_for(dev, stream, C.workspace_size(w.batch, w.vocab, C.DTYPE_F16, w.hist_max_len))
+    f = packed.f32
+    C.sample(lg.data_ptr(), C.DTYPE_F16, w.batch, w.vocab, w.vocab, f[0].data_ptr(), f[1].data_ptr(),
+             packed.top_k.data_ptr(), u.data_ptr(), out.data_ptr(), status=status.data_ptr(),
+             repetition_penalty=f[2].data_ptr(), presence_penalty=f[3].data_ptr(),
+             frequency_penalty=f[4].data_ptr(), greedy=packed.greedy.data_ptr(), hist_ids=hid.data_ptr(),
+             hist_offsets=hoff.data_ptr(), hist_max_len=w.hist_max_len, workspace=ws.data_ptr(),
+             workspace_bytes=ws.numel() * 4, stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    compare(w, _oracle(w), out.cpu().numpy(), status.cpu().numpy(), None)
