@@ -184,21 +184,18 @@ int fg_sample_candidates(const FgSampleArgs* args, float* vals, int32_t* gids,
                          int32_t* counts, int32_t cand_max, void* stream);
 
 /*
- * Small-batch split path of fg_sample (no reference counterpart; FlashGen
- * samples one row per call on the CPU). When a batch leaves most SMs idle,
- * each row's columns are cut into G shards (G a power of two dividing vocab)
- * sampled by G CTAs: per shard the candidates after penalties and temperature
- * and a mass partial, then one merge per row that draws from the union with
- * the whole row's mass, then a fixup launch that samples whole any row the
- * union could not decide exactly (a cut or draw below the union's complete
- * part, a shard error). The kept set and the draw order are the unsplit
- * path's; integer masses are rounded at another scale and the row total is
- * summed in another order, so a draw may differ only where the uniform lies
- * within rounding of a CDF boundary (the parity tolerance). mode 0 turns it
- * off, 1 (default) uses it when B * G <= SMs and vocab / G >= 4096, 2 uses it
- * whenever the shapes allow (tests). Process-wide; returns FG_EINVAL for other
- * modes. Not used by fg_sample_candidates or fg_sample_noalloc, nor with
- * out_probs, vocab shards (vocab_offset, vocab_total) or padded rows.
+ * Small-batch mode of fg_sample (no reference counterpart; FlashGen samples
+ * one row per call on the CPU). A batch of a few rows would leave most SMs
+ * idle with one CTA per row, so fg_sample samples it with the cluster kernel
+ * instead: one thread-block cluster of G CTAs (G <= 16) per row, each CTA
+ * keeping a slice of the row's keys in shared memory, the decisions reduced
+ * across the cluster through distributed shared memory. Same kept set, draw
+ * order and integer masses as the batch path. mode 0 never takes it for a
+ * whole batch, 1 (default) takes it when B * G <= SMs with G >= 4, 2 takes it
+ * for every batch (tests). Calls that want kept-set probabilities (out_probs)
+ * and rows the batch path hands on always use the cluster kernel.
+ * Process-wide (an atomic, read once per call); returns FG_EINVAL for other
+ * modes.
  */
 int fg_sample_set_split(int mode);
 
