@@ -64,7 +64,7 @@ int launch_all(strm::Params& P, int k2_smem, int k2_grid, int k1_smem, int k3_sm
         // K4: 16-bit rows whose top-p cut or draw lies below the candidates
         rc = set_smem_attr(strm::deep_kernel<DT>, d, K_DEEP, DT);
         if (rc != FG_OK) return rc;
-        strm::deep_kernel<DT><<<k3_grid, strm::NCT, k4_smem, st>>>(P);
+        strm::deep_kernel<DT><<<k3_grid, strm::DNT, k4_smem, st>>>(P);
         if (cudaGetLastError() != cudaSuccess) return FG_ELAUNCH;
     } else {
         (void)k4_smem;

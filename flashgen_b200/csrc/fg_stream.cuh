@@ -1403,7 +1403,9 @@ constexpr int NBIN = 16384;            // slots of the 16-bit keys counted below
 constexpr int SLOTS = NBIN / NCT;      // keys per thread range of the scan (<= NCT)
 static_assert(SLOTS <= NCT, "one key per thread inside a range");
 constexpr int HL_MAX = 64;             // history entries whose value lies in one key's cell
-constexpr int DCH = 8;                 // K4: 16-byte chunks a thread loads at a time (DCH * VEC <= 64)
+constexpr int DCH = 8;                 // K4 column pass: 16-byte chunks a thread loads at a time (DCH * VEC <= 64)
+constexpr int DCH1 = 4;                // K4 counting pass: chunks a thread loads at a time
+constexpr int DNT = 1024;              // K4 threads (set-up, counting, masses); NCT of them do the rest
 constexpr int kDeepStaticSmem = 4096;  // bound on K4's static shared memory (scan buffer, control)
 
 __device__ __forceinline__ uint32_t key16_of_bits(uint32_t u) { return (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u); }
@@ -1513,7 +1515,7 @@ __device__ __noinline__ int64_t cand_draw(const Sm& s, uint32_t n, float My, flo
 }
 
 template <int DT>
-__global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(DNT, 1) deep_kernel(const __grid_constant__ Params P) {
     using E = Elem<DT>;
     constexpr int VEC = E::VEC;
     const Sm s = carve(P);
@@ -1549,17 +1551,18 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
         const int ktop = ktop_raw < 0 ? -1 : (int)VK<DT>::of((uint32_t)ktop_raw);   // its slot
         const int klo = ktop - (NBIN - 1);              // may be negative: those bins stay empty
         // ---- bitmap of the history columns; counters cleared ----
+        // (set-up, counting and masses use all DNT threads; the scans and the
+        // draw the first NCT, on the consumer-group barrier)
         if (P.pen_possible)
-            for (int i = tid; i <= P.nwords; i += NCT) s.hbm[i] = 0u;
-        for (int i = tid; i < NBIN; i += NCT) cnt[i] = 0u;
-        for (int i = tid; i < NCT; i += NCT) tsum[i] = 0ull;
+            for (int i = tid; i <= P.nwords; i += DNT) s.hbm[i] = 0u;
+        for (int i = tid; i < NBIN; i += DNT) cnt[i] = 0u;
         if (tid == 0) { dc.flag = ktop < 0 ? 1 : 0; dc.found = 0; dc.nh = 0u; s.ctl->ovf = 0u; }
-        csync();
-        for (uint32_t i = tid; i < U; i += NCT) {
+        __syncthreads();
+        for (uint32_t i = tid; i < U; i += DNT) {
             const uint32_t c = __ldcg(hc + i);
             atomicOr(&s.hbm[c >> 5], 1u << (c & 31u));
         }
-        csync();
+        __syncthreads();
         // ---- pass 1: counts of the non-history 16-bit values below tau ----
         auto count_elem = [&](uint32_t bits16) {
             // below tau iff the key is (keys are order-preserving)
@@ -1570,16 +1573,16 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
         };
         const int64_t nchunks = g.ibytes / 16;
         const uint4* gin = reinterpret_cast<const uint4*>(g.interior);
-        for (int64_t base = 0; base < nchunks; base += DCH * NCT) {
-            uint4 v[DCH];
+        for (int64_t base = 0; base < nchunks; base += DCH1 * DNT) {
+            uint4 v[DCH1];
 #pragma unroll
-            for (int j = 0; j < DCH; ++j) {   // every load in flight before the counting
-                const int64_t ch = base + j * NCT + tid;
+            for (int j = 0; j < DCH1; ++j) {   // every load in flight before the counting
+                const int64_t ch = base + j * DNT + tid;
                 v[j] = ch < nchunks ? __ldg(gin + ch) : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
-            for (int j = 0; j < DCH; ++j) {
-                const int64_t ch = base + j * NCT + tid;
+            for (int j = 0; j < DCH1; ++j) {
+                const int64_t ch = base + j * DNT + tid;
                 if (ch >= nchunks) continue;
                 const int c0 = g.head + (int)ch * VEC;
                 const uint32_t hb = p.pen ? hist_bits<VEC>(s.hbm, (uint32_t)c0) : 0u;
@@ -1593,21 +1596,31 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
         }
         {
             const int nh = g.head, ntl = P.vocab - g.tail0;
-            for (int i = tid; i < nh + ntl; i += NCT) {
+            for (int i = tid; i < nh + ntl; i += DNT) {
                 const int c = i < nh ? i : g.tail0 + (i - nh);
                 if (p.pen && hist_bit(s.hbm, (uint32_t)c)) continue;
                 count_elem(reinterpret_cast<const uint16_t*>(g.row)[c]);
             }
         }
-        csync();
+        __syncthreads();
         // ---- masses per thread's keys (descending order: thread NCT-1 holds the largest) ----
-        // keys interleaved over the threads (populated keys come in runs), each
-        // key's mass added to the sum of its range of SLOTS keys
-        for (int k = tid; k < NBIN; k += NCT) {
-            const uint32_t c = cnt[k];
-            if (c) atomicAdd(&tsum[k / SLOTS],
-                             (unsigned long long)c * qmass(ydiv(p, val16<DT>(VK<DT>::key((uint32_t)(k + klo)))), My, scale));
+        // the mass of each range of SLOTS keys: one warp per range, its lanes
+        // over the range's keys, a shuffle reduction (no atomics)
+        {
+            const int lane = tid & 31;
+            for (int rg = tid >> 5; rg < NCT; rg += DNT / 32) {
+                unsigned long long m = 0;
+                for (int k = rg * SLOTS + lane; k < (rg + 1) * SLOTS; k += 32) {
+                    const uint32_t c = cnt[k];
+                    if (c) m += (unsigned long long)c * qmass(ydiv(p, val16<DT>(VK<DT>::key((uint32_t)(k + klo)))), My, scale);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
+                if (lane == 0) tsum[rg] = m;
+            }
         }
+        __syncthreads();
+        if (tid < NCT) {   // the rest of the row runs on the first NCT threads
         // history entries below tau, each with its own mass, at the key just below or at its value
         for (uint32_t i = tid; i < U; i += NCT) {
             const float v = hp[i];
@@ -1869,6 +1882,8 @@ __global__ void __launch_bounds__(NCT) deep_kernel(const __grid_constant__ Param
             }
         }
         csync();
+        }
+        __syncthreads();   // every thread, before the next row reuses shared memory
     }
 }
 
