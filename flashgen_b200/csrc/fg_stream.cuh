@@ -1,11 +1,11 @@
 // fg_stream.cuh — the batch path of fg_sample (sm_100a): three kernels per call.
 //
 //   K1 prep_kernel     one CTA per row with penalties: the row's distinct history
-//                      columns with their counts, raw logits and penalised
-//                      values (FlashGen's repetition penalty, plus presence and
-//                      frequency), written to the row's workspace block; the
-//                      best penalised value (greedy rows) and the NaN-propagating
-//                      maximum of the penalised values.
+//                      columns with their counts, written to the row's
+//                      workspace block (K2 gathers their raw logits right after
+//                      streaming the row, from L2, and writes their penalised
+//                      values: FlashGen's repetition penalty, plus presence and
+//                      frequency; their best value and NaN-propagating maximum).
 //   K2 stream_kernel   persistent CTAs, two per SM, each a producer warp and
 //                      NCW consumer warps. The producer takes rows from a global
 //                      queue (rows that sum exp over the whole row first) and
@@ -54,7 +54,7 @@ constexpr int64_t kPendingId = -3;      // out_ids of a row K2 leaves to K3
 constexpr int64_t kDeepId = -4;         // out_ids of a row K3 leaves to K4
 
 // Per-row workspace block (16-byte aligned parts):
-//   RowStat, HistHdr, hcol[hu_cap], hraw[hu_cap], hpen[hu_cap], ckey[cap], ccol[cap]
+//   RowStat, HistHdr, hcol[hu_cap], hcnt[hu_cap], hpen[hu_cap], ckey[cap], ccol[cap]
 struct RowStat {
     double zr;        // sum over the raw row of 2^((x - mraw) * c)
     float mraw;       // NaN-propagating maximum of the raw row
@@ -71,9 +71,9 @@ struct RowStat {
 struct HistHdr {
     uint32_t nh;      // distinct history columns kept (<= hu_cap)
     uint32_t flags;   // FG_ROW_BAD_HISTORY / FG_ROW_BAD_PARAM
-    float pbest;      // best penalised history value and its first column
+    float pbest;      // best penalised history value and its first column (K2)
     uint32_t pcol;
-    float hmax;       // NaN-propagating maximum of the penalised history values
+    float hmax;       // NaN-propagating maximum of the penalised history values (K2)
     uint32_t pad[3];
 };
 __host__ __device__ inline int64_t wrow_bytes(int hu_cap, int cap) {
@@ -124,9 +124,7 @@ __device__ __forceinline__ HistHdr* hist_hdr(const Params& P, int r) {
 __device__ __forceinline__ uint32_t* g_hcol(const Params& P, int r) {
     return reinterpret_cast<uint32_t*>(P.wrow + (int64_t)r * P.wrow_bytes + sizeof(RowStat) + sizeof(HistHdr));
 }
-__device__ __forceinline__ float* g_hraw(const Params& P, int r) {
-    return reinterpret_cast<float*>(g_hcol(P, r) + P.hcap4);
-}
+__device__ __forceinline__ uint32_t* g_hcnt(const Params& P, int r) { return g_hcol(P, r) + P.hcap4; }
 __device__ __forceinline__ float* g_hpen(const Params& P, int r) {
     return reinterpret_cast<float*>(g_hcol(P, r) + 2 * P.hcap4);
 }
@@ -468,8 +466,9 @@ __device__ __forceinline__ bool hist_bit(const uint32_t* bm, uint32_t c) { retur
 // K1: history of every row with penalties
 // ===========================================================================
 // Distinct history columns with their counts (open-addressed hash; the work
-// follows the history, not the vocabulary), their raw logits and penalised
-// values, the best penalised value and the NaN-propagating maximum.
+// follows the history, not the vocabulary). No logit is read here: a scattered
+// gather would pull a whole line from HBM per column, while K2 finds the row
+// in L2 right after streaming it.
 template <int DT>
 __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Params P) {
     using E = Elem<DT>;
@@ -484,7 +483,6 @@ __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Param
         if (tid == 0) { hh->nh = 0u; hh->flags = 0u; hh->pbest = -INFINITY; hh->pcol = 0xffffffffu; hh->hmax = -INFINITY; }
         return;
     }
-    const Geom g = row_geom<E::SIZE>(P.logits, P.row_stride, P.vocab, r);
     // shared memory: the count hash, then the distinct columns (sort buffer)
     uint32_t* hkey = reinterpret_cast<uint32_t*>(ssmem + P.off_ctl + sizeof(Ctl));
     uint32_t* hcnt = hkey + P.hslots;
@@ -520,10 +518,7 @@ __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Param
     const uint32_t total = ctl->nuniq;
     const uint32_t U = min(total, (uint32_t)P.hu_cap);
     uint32_t* hc = g_hcol(P, r);
-    float* hr = g_hraw(P, r);
-    float* hp = g_hpen(P, r);
-    float bv = -INFINITY, hm = -INFINITY;
-    uint32_t bc = 0xffffffffu;
+    uint32_t* hn = g_hcnt(P, r);
     for (uint32_t i = tid; i < U; i += NCT) {
         const uint32_t c = srt[i];
         uint32_t h = col_hash(c, mask), count = 0;
@@ -531,35 +526,14 @@ __global__ void __launch_bounds__(NCT) prep_kernel(const __grid_constant__ Param
             if (hkey[h] == c) { count = hcnt[h]; break; }
             h = (h + 1u) & mask;
         }
-        const float raw = E::load(g.row, c);
-        const float pen = penalize(p, raw, count);
-        hc[i] = c; hr[i] = raw; hp[i] = pen;
-        hm = fmax_nan(hm, pen);
-        if (arg_better(pen, c, bv, bc)) { bv = pen; bc = c; }
+        hc[i] = c; hn[i] = count;
     }
-    hm = c_max_nan(hm, s);
-    // the best penalised value (first column on ties)
-    const int lane = tid & 31, wid = tid >> 5;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
-        const uint32_t c2 = __shfl_xor_sync(0xffffffffu, bc, o);
-        if (arg_better(v2, c2, bv, bc)) { bv = v2; bc = c2; }
-    }
-    if (lane == 0) { ctl->redf[wid] = bv; ctl->red32b[wid] = bc; }
     __syncthreads();
     if (tid == 0) {
-        float v = ctl->redf[0];
-        uint32_t c = ctl->red32b[0];
-        for (int i = 1; i < NCW; ++i)
-            if (arg_better(ctl->redf[i], ctl->red32b[i], v, c)) { v = ctl->redf[i]; c = ctl->red32b[i]; }
         uint32_t fl = (uint32_t)ctl->status;
         if (total > (uint32_t)P.hu_cap) fl |= FG_ROW_BAD_PARAM;
         hh->nh = U;
         hh->flags = fl;
-        hh->pbest = v;
-        hh->pcol = c;
-        hh->hmax = hm;
     }
 }
 
@@ -929,6 +903,29 @@ __device__ __noinline__ void sample_row_cls(const Params& P, int r, Ring& rg) {
             }
         }
     }
+    if (PEN) {
+        // the history columns' raw values, right after the row streamed through
+        // L2, penalised with K1's counts; their maximum and best entry
+        const uint32_t U = min(hist_hdr(P, r)->nh, (uint32_t)P.hu_cap);
+        const uint32_t* hc = g_hcol(P, r);
+        const uint32_t* hn = g_hcnt(P, r);
+        float* hp = g_hpen(P, r);
+        float hm = -INFINITY, pb = -INFINITY;
+        uint32_t pc = 0xffffffffu;
+        for (uint32_t i = tid; i < U; i += NCT) {
+            const uint32_t c = __ldcg(hc + i);
+            const float pen = penalize(p, E::load(g.row, c), __ldcg(hn + i));
+            hp[i] = pen;
+            hm = fmax_nan(hm, pen);
+            if (arg_better(pen, c, pb, pc)) { pb = pen; pc = c; }
+        }
+        hm = c_max_nan(hm, s);
+        c_argmax(pb, pc, s);
+        if (tid == 0) {
+            HistHdr* hw = hist_hdr(P, r);
+            hw->hmax = hm; hw->pbest = pb; hw->pcol = pc;
+        }
+    }
     csync();
     const bool ovf = s.ctl->ovf != 0u;
     const uint32_t n = min(s.ctl->ncand, (uint32_t)P.cap);
@@ -1273,7 +1270,7 @@ __device__ __noinline__ Fin finish_sampling(const Params& P, int r, uint32_t n, 
 // K3: decide the rows K2 left (out_ids == kPendingId)
 // ===========================================================================
 template <int DT>
-__global__ void __launch_bounds__(NCT) decide_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(NCT, 5) decide_kernel(const __grid_constant__ Params P) {
     const Sm s = carve(P);
     const int tid = threadIdx.x;
     for (int r = blockIdx.x; r < P.batch; r += gridDim.x) {
@@ -1750,18 +1747,18 @@ __global__ void __launch_bounds__(DNT, 1) deep_kernel(const __grid_constant__ Pa
                 const int64_t ch0 = t0 + (int64_t)tid * DCH;
                 uint4 v[DCH];
 #pragma unroll
-                for (int j = 0; j < DCH; ++j)
-                    v[j] = ch0 + j < nchunks ? __ldg(gin + ch0 + j) : make_uint4(0u, 0u, 0u, 0u);
+                for (int q = 0; q < DCH; ++q)
+                    v[q] = ch0 + q < nchunks ? __ldg(gin + ch0 + q) : make_uint4(0u, 0u, 0u, 0u);
                 uint32_t m = 0u;
-                unsigned long long mm = 0ull;   // matches; bit j*VEC+e of mm (DCH * VEC <= 64)
+                unsigned long long mm = 0ull;   // matches; bit q*VEC+e of mm (DCH * VEC <= 64)
 #pragma unroll
-                for (int j = 0; j < DCH; ++j) {
-                    if (ch0 + j >= nchunks) continue;
-                    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-                    const int c0 = g.head + (int)(ch0 + j) * VEC;
+                for (int q = 0; q < DCH; ++q) {
+                    if (ch0 + q >= nchunks) continue;
+                    const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+                    const int c0 = g.head + (int)(ch0 + q) * VEC;
 #pragma unroll
                     for (int e = 0; e < VEC; ++e)
-                        if (match(c0 + e, (w[e >> 1] >> (16 * (e & 1))) & 0xffffu)) { mm |= 1ull << (j * VEC + e); ++m; }
+                        if (match(c0 + e, (w[e >> 1] >> (16 * (e & 1))) & 0xffffu)) { mm |= 1ull << (q * VEC + e); ++m; }
                 }
                 // exclusive scan of m in thread order
                 const int lane = tid & 31, wid = tid >> 5;
