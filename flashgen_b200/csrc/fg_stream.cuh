@@ -824,8 +824,8 @@ __device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st
     St st = st_io;
     volatile int* abort = &s.ctl->abort;
     // the buffer holds non-history columns only: compactions keep kt entries.
-    // The count is checked after every tile; a compaction starts while a
-    // quarter of the buffer is still free, so a tile rarely overflows it.
+    // The count is checked after every second tile; a compaction starts while a
+    // quarter of the buffer is still free, so two tiles rarely overflow it.
     const int kt2 = min(kt, P.cap / 2);
     uint32_t trig = (uint32_t)min(P.cap * 3 / 4, max(2 * kt2 + 256, 512));
     for (int t = 0; t < nt; ++t) {
@@ -847,7 +847,7 @@ __device__ __noinline__ void stream_row(const Params& P, int r, Ring& rg, St& st
         if (CLS != RC_GREEDY && t == 0) st.tau = tile0_tau<DT>(P, kt, nch, v[0], v[1], v[2], v[3]);
         tile_chunks<DT, CLS, PEN>(P, s, v, nch, tcol0, st);
         if (CLS != RC_GREEDY) {
-            {
+            if ((t & 1) || t == nt - 1) {
                 csync();
                 const uint32_t n = s.ctl->ncand;
                 const bool ovf = s.ctl->ovf != 0u;
