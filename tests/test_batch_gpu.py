@@ -120,3 +120,40 @@ def test_pybind_sample_matches_oracle(cuda_device):
              workspace_bytes=ws.numel() * 4, stream=stream.cuda_stream)
     torch.cuda.synchronize()
     compare(w, _oracle(w), out.cpu().numpy(), status.cpu().numpy(), None)
+
+
+def test_decode_batch_steps(cuda_device):
+    """Several decode steps through DecodeBatch (device-resident histories,
+    one fg_sample call per step, ids appended on the device): every step's ids
+    against the oracle with the histories as they stood before that step."""
+    from flashgen_b200.core.config import SamplingParams
+    from flashgen_b200.sampling.decode import DecodeBatch
+
+    rng = np.random.default_rng(12)
+    B, V, steps = 64, 32000, 4
+    params = [SamplingParams(temperature=float(rng.uniform(0.6, 1.1)), top_p=float(rng.uniform(0.8, 0.99)),
+                             top_k=int(rng.choice([-1, 20, 100])), repetition_penalty=float(rng.uniform(1.0, 1.3)),
+                             presence_penalty=float(rng.uniform(0, 0.3)), frequency_penalty=float(rng.uniform(0, 0.2)))
+              for _ in range(B)]
+    dec = DecodeBatch(params, vocab=V, capacity=256, device=cuda_device)
+    for r in range(B):
+        dec.set_history(r, rng.integers(0, V, int(rng.integers(0, 200))).tolist())
+    bp = BatchParams(*(np.array([getattr(p, f) for p in params], dtype=dt) for f, dt in (
+        ("temperature", np.float32), ("top_p", np.float32), ("top_k", np.int32), ("repetition_penalty", np.float32),
+        ("presence_penalty", np.float32), ("frequency_penalty", np.float32), ("greedy", bool))))
+    for s in range(steps):
+        x = rng.standard_normal((B, V), dtype=np.float32)
+        x[:, rng.integers(0, V, 40)] += 5.0
+        logits = torch.from_numpy(x).to(torch.float16)
+        u = rng.random(B, dtype=np.float32)
+        before = dec.histories()
+        ids = dec.step(logits.to(cuda_device), uniforms=torch.from_numpy(u).to(cuda_device))
+        torch.cuda.synchronize()
+        got = ids.cpu().numpy()
+        offs = np.zeros(B + 1, np.int64)
+        offs[1:] = np.cumsum([len(h) for h in before])
+        hid = np.concatenate([np.asarray(h, np.int32) for h in before]) if offs[-1] else np.zeros(0, np.int32)
+        w = Workload(0, "decode", logits, bp, hid, offs, u)
+        compare(w, _oracle(w), got, dec.status.cpu().numpy(), None)
+        after = dec.histories()
+        assert all(a == b + [int(i)] for a, b, i in zip(after, before, got))
