@@ -100,7 +100,7 @@ int stream_launch(const FgSampleArgs* a, int64_t vtot, bool pen_possible, int hu
     P.mass_shift = 62 - bits_for(a->vocab);
     P.cap = kCap;
     P.k_fast = kCap / 2;
-    P.k_nuc = kCap * 3 / 8;
+    P.k_nuc = kCap / 3;
     // the workspace holds a block per row after the counters
     P.wrow_bytes = strm::wrow_bytes(P.hu_cap, P.cap);
     const size_t need = 256 + (size_t)a->batch * (size_t)P.wrow_bytes;
