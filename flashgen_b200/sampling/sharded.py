@@ -112,23 +112,23 @@ def merge_and_draw(vals: torch.Tensor, gids: torch.Tensor, shard_status: torch.T
 def exchange(c: Candidates, world: int, group=None) -> Candidates:
     """All-to-all by row owner: rank h receives, for its B/G rows, every
     shard's candidates; returns [B/G, G*cmax] vals/gids and the OR of the
-    shards' status words."""
+    shards' status words. One NCCL all-to-all carries everything: each row
+    is packed as [value bits (cmax), global ids (cmax), status] int32 words."""
     import torch.distributed as dist
     B, cmax = c.vals.shape
     if B % world:
         raise ValueError(f"batch {B} is not a multiple of the world size {world}")
     Bo = B // world
     # send buffer: rows already grouped by owner (contiguous row blocks)
-    rv = torch.empty_like(c.vals)
-    rg = torch.empty_like(c.gids)
-    rs = torch.empty_like(c.status)
-    dist.all_to_all_single(rv, c.vals.contiguous(), group=group)
-    dist.all_to_all_single(rg, c.gids.contiguous(), group=group)
-    dist.all_to_all_single(rs, c.status.contiguous(), group=group)
-    # received: [world (source shard), Bo, cmax] -> [Bo, world * cmax]
-    vals = rv.view(world, Bo, cmax).permute(1, 0, 2).reshape(Bo, world * cmax)
-    gids = rg.view(world, Bo, cmax).permute(1, 0, 2).reshape(Bo, world * cmax)
-    status = rs.view(world, Bo)
+    send = torch.cat([c.vals.contiguous().view(torch.int32), c.gids.contiguous(),
+                      c.status.contiguous().view(B, 1)], dim=1)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    # received: [world (source shard), Bo, 2 * cmax + 1]
+    r = recv.view(world, Bo, 2 * cmax + 1)
+    vals = r[:, :, :cmax].contiguous().view(torch.float32).permute(1, 0, 2).reshape(Bo, world * cmax)
+    gids = r[:, :, cmax:2 * cmax].permute(1, 0, 2).reshape(Bo, world * cmax)
+    status = r[:, :, 2 * cmax]
     st = status[0].clone()
     for i in range(1, world):
         st |= status[i]
