@@ -58,8 +58,8 @@ namespace {
 constexpr int32_t kMaxBatch = 1 << 30;
 
 // Shared-memory layout for P (vocab, pen_possible, hu_cap set), then the
-// launch. mass_vocab: how many elements a row's total mass may sum (the merge
-// of the split path sums a whole row's mass over a shorter union row).
+// launch of fg_sample_kernel (fg_sample_candidates). mass_vocab: how many
+// elements a row's total mass may sum (0: the row's own vocabulary).
 int layout_and_launch(fg::KParams& P, int dtype, DevInfo* d, cudaStream_t st, int64_t mass_vocab = 0) {
     P.id_bits = bits_for(std::max<int64_t>(P.vocab, mass_vocab));
     P.mass_shift = 62 - P.id_bits;

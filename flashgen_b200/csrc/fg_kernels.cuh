@@ -1,6 +1,14 @@
 // fg_kernels.cuh — kernels behind the C ABI in include/flashgen_sampler.h.
 //
-//   fg_sample_kernel<DT>      fused penalties/temperature/top-k/top-p/draw
+//   fg_sample_kernel<DT>      one persistent CTA per row: fused penalties /
+//                             temperature / top-k, launched by
+//                             fg_sample_candidates (the local stage of
+//                             vocabulary-sharded sampling). fg_sample itself
+//                             runs the batch kernels (fg_stream.cuh) and the
+//                             cluster kernel (fg_cluster.cuh). The kernel's
+//                             shard / merge / fixup stages (KParams nshard,
+//                             merge_g, redo) served an earlier small-batch
+//                             path and are not launched by any entry point.
 //   fg_argmax_kernel<DT>      row argmax (torch.argmax semantics)
 //   fg_rep_penalty_kernel<DT> in-place repetition penalty
 #pragma once

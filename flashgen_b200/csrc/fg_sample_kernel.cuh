@@ -81,8 +81,10 @@ struct KParams {
     int32_t pen_possible;
     int32_t mass_shift;      // S: masses are round(e * 2^S)
     int32_t id_bits;         // bits needed for a column index
-    // ---- split path for small batches: each row's columns are cut into
-    //      nshard shards sampled by different CTAs, whose candidates are merged
+    // ---- shard / merge / fixup stages of an earlier small-batch path (no
+    //      entry point launches them: zero / null in every KParams built by
+    //      fg_abi.cu): each row's columns cut into nshard shards sampled by
+    //      different CTAs, whose candidates are merged
     // shard stage (nshard > 1): launch row r is shard r % nshard of row
     // r / nshard, columns [(r % nshard) * vocab, ... + vocab); candidates mode
     // with the outputs below, sorted by column

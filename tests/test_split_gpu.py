@@ -1,8 +1,8 @@
-"""Small-batch split path of fg_sample: rows cut into column shards sampled by
-several CTAs, merged per row, and any row the merge cannot decide exactly
-sampled whole. Token ids must equal the oracle's on every row it does not flag
-(and the unsplit kernel's, which rounds masses at another scale, on the same
-rows)."""
+"""Small batches of fg_sample: a batch that would leave most SMs idle with one
+CTA per row is sampled by the cluster kernel, one thread-block cluster per row
+(fg_sample_set_split picks it: 0 never, 1 when it pays, 2 always). Token ids
+must equal the oracle's on every row it does not flag, and the cluster
+kernel's ids must equal the batch path's on the same rows."""
 import numpy as np
 import pytest
 import torch
