@@ -21,14 +21,14 @@ using fg::host::g_mu;
 template <int DT>
 int launch_sample(const fg::KParams& P, int smem, int grid, cudaStream_t st, DevInfo* d) {
     auto kern = fg::fg_sample_kernel<DT>;
-    if (!d->attr_set[fg::host::K_ROW][DT]) {
+    if (!d->attr_set[fg::host::K_ROW][DT].load(std::memory_order_acquire)) {
         std::lock_guard<std::mutex> lk(g_mu);
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->smem_optin) != cudaSuccess)
             return FG_EDEVICE;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return FG_EDEVICE;
-        d->attr_set[fg::host::K_ROW][DT] = true;
+        d->attr_set[fg::host::K_ROW][DT].store(true, std::memory_order_release);
     }
     kern<<<grid, fg::NTHREADS, smem, st>>>(P);
     return cudaGetLastError() == cudaSuccess ? FG_OK : FG_ELAUNCH;

@@ -46,12 +46,12 @@ static int launch_cluster_t(const fg::clus::Params& P, int G, int smem, int nclu
         // attributes once per device; the co-resident cluster count once per
         // (dtype, cluster size, shared-memory size)
         std::lock_guard<std::mutex> lk(g_mu);
-        if (!d->attr_set[K_CLUSTER][DT]) {
+        if (!d->attr_set[K_CLUSTER][DT].load(std::memory_order_acquire)) {
             if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d->smem_optin) != cudaSuccess)
                 return FG_EDEVICE;
             if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
                 return FG_EDEVICE;
-            d->attr_set[K_CLUSTER][DT] = true;
+            d->attr_set[K_CLUSTER][DT].store(true, std::memory_order_release);
         }
         if (d->cl_smem[DT][G] != smem || d->cl_active[DT][G] < 1) {
             if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess || active < 1) return FG_ENOTSUP;

@@ -3,6 +3,7 @@
 // kernel; fg_stream.cu: the batch kernel). Not part of the public ABI.
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <mutex>
@@ -18,8 +19,9 @@ struct DevInfo {
     int sms = 0;
     int smem_optin = 0;
     int smem_per_sm = 0;
-    // one-time kernel attributes, per kernel family (see the K_* ids) and dtype
-    bool attr_set[6][3] = {};
+    // one-time kernel attributes, per kernel family (see the K_* ids) and
+    // dtype: read without the lock (acquire), set under it (release)
+    std::atomic<bool> attr_set[6][3] = {};
     // cluster kernel: co-resident clusters per (dtype, cluster size) for the
     // shared-memory size it was last queried with
     int cl_smem[3][17] = {};

@@ -17,8 +17,9 @@ constexpr int kMinStages = 3;
 
 template <class K>
 int set_smem_attr(K kern, DevInfo* d, int family, int dt) {
-    if (d->attr_set[family][dt]) return FG_OK;
+    if (d->attr_set[family][dt].load(std::memory_order_acquire)) return FG_OK;
     std::lock_guard<std::mutex> lk(g_mu);
+    if (d->attr_set[family][dt].load(std::memory_order_relaxed)) return FG_OK;
     // the dynamic share of the opt-in limit: what the kernel's static shared memory leaves
     cudaFuncAttributes fa{};
     if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return FG_EDEVICE;
@@ -28,7 +29,7 @@ int set_smem_attr(K kern, DevInfo* d, int family, int dt) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                              (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
         return FG_EDEVICE;
-    d->attr_set[family][dt] = true;
+    d->attr_set[family][dt].store(true, std::memory_order_release);
     return FG_OK;
 }
 
